@@ -1,0 +1,133 @@
+/*
+ * aotk.h - C ABI of the B200 (sm_100a) dense-linear inference kernels.
+ *
+ * Every entry point takes plain device pointers, element counts and a CUDA
+ * stream handle (cudaStream_t passed as void*, NULL = legacy default stream),
+ * launches asynchronously on that stream and returns a status code.  No entry
+ * point allocates device memory, synchronises the device or keeps state
+ * between calls apart from per-device launch configuration set up on first
+ * use.  Pointers must belong to the current device (cudaSetDevice).
+ *
+ * The operator names mirror the reference's torch operator library
+ * (aot_kernel/csrc/registration.cc:10-25 of gongyisheng/inference-kernel):
+ * each aotk_<op> is what the TORCH_LIBRARY kernel <op> does once its tensors
+ * are reduced to pointers, so a torch binding is a thin adapter (see
+ * aot_kernel/csrc/registration.cc in this package) and a non-torch caller
+ * binds the same symbols through ctypes / cffi / dlopen.
+ *
+ * Layouts: all matrices are row-major and dense in the last dimension.
+ * GEMM: C[M,N] = A[M,K] * B[K,N], 16-bit inputs, fp32 accumulation, one
+ * rounding to the output type (the contract of ref.gemm = `a @ b`,
+ * ref/gemm.py:4-5).
+ */
+#ifndef AOTK_H_
+#define AOTK_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define AOTK_API __attribute__((visibility("default")))
+#else
+#define AOTK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types. */
+enum aotk_dtype {
+  AOTK_FLOAT32 = 0,
+  AOTK_FLOAT16 = 1,
+  AOTK_BFLOAT16 = 2
+};
+
+/* Status codes returned by every entry point. */
+enum aotk_status {
+  AOTK_OK = 0,
+  AOTK_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, bad stride   */
+  AOTK_ERR_UNSUPPORTED = 2,      /* dtype / alignment this entry cannot serve  */
+  AOTK_ERR_CUDA = 3,             /* a CUDA runtime call failed                 */
+  AOTK_ERR_DEVICE = 4            /* current device is not an sm_100 part       */
+};
+
+/* Message describing the last non-OK status returned on the calling thread. */
+AOTK_API const char* aotk_last_error(void);
+
+/* Library version, major * 10000 + minor * 100 + patch. */
+AOTK_API int aotk_version(void);
+
+/* ---- activation -------------------------------------------------------- */
+
+/* out[i] = x[i] / (1 + exp(-x[i])), computed in fp32, rounded once.
+ * Replaces silu_forward(Tensor! out, Tensor x)
+ * (aot_kernel/csrc/activation/silu.cu:22-41, registration.cc:14-15). */
+AOTK_API int aotk_silu_forward(void* out, const void* x, int64_t n, int dtype, void* stream);
+
+/* out[i] = max(x[i], 0).
+ * Replaces relu_forward(Tensor! out, Tensor x)
+ * (aot_kernel/csrc/activation/relu.cu:22-41, registration.cc:11-12). */
+AOTK_API int aotk_relu_forward(void* out, const void* x, int64_t n, int dtype, void* stream);
+
+/* out[r, c] = silu(gate[r, c]) * up[r, c] for r < rows, c < cols, computed in
+ * fp32 and rounded once.  *_stride are element strides between rows, so gate
+ * and up may be the two column halves of one fused [rows, 2*cols] GEMM output.
+ * No reference counterpart: the reference composes ref.silu(gate) * up
+ * (ref/activation.py:15-16). */
+AOTK_API int aotk_silu_mul_forward(void* out, int64_t out_stride, const void* gate, int64_t gate_stride,
+                          const void* up, int64_t up_stride, int64_t rows, int64_t cols,
+                          int dtype, void* stream);
+
+/* ---- norm ------------------------------------------------------------- */
+
+/* out[r, :] = x[r, :] * rsqrt(mean(x[r, :]^2) + eps) * weight, fp32 math,
+ * one rounding; x is [rows, cols] dense, weight is [cols].
+ * Replaces rmsnorm_forward(Tensor! out, Tensor x, Tensor weight, float eps)
+ * (aot_kernel/csrc/norm/rmsnorm.cu:185-239, registration.cc:17-18). */
+AOTK_API int aotk_rmsnorm_forward(void* out, const void* x, const void* weight, int64_t rows,
+                         int64_t cols, double eps, int dtype, void* stream);
+
+/* ---- gemm ------------------------------------------------------------- */
+
+/* Tensor-core GEMM for FLOAT16 / BFLOAT16 (FLOAT32 returns AOTK_ERR_UNSUPPORTED,
+ * as the reference's gemm_opt rejects it).  Picks the persistent tcgen05
+ * kernel, the skinny split-K tcgen05 kernel (M <= 128) or, for shapes TMA
+ * cannot address (K or N not a multiple of 8, pointers not 16-byte aligned),
+ * the SIMT kernel.
+ * Replaces gemm_opt(Tensor! out, Tensor a, Tensor b)
+ * (aot_kernel/csrc/gemm/gemm_opt.cu:165-195, registration.cc:23-24). */
+AOTK_API int aotk_gemm_opt(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
+                  int dtype, void* stream);
+
+/* Any-dtype, any-shape GEMM (SIMT, fp32 accumulation).
+ * Replaces gemm(Tensor! out, Tensor a, Tensor b)
+ * (aot_kernel/csrc/gemm/gemm.cu:106-157, registration.cc:20-21). */
+AOTK_API int aotk_gemm(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
+              int dtype, void* stream);
+
+/* Path-pinned variants of aotk_gemm_opt, for tests and benchmarks that must
+ * exercise one kernel.  They return AOTK_ERR_UNSUPPORTED where the kernel's
+ * preconditions (listed with each) do not hold instead of falling back. */
+
+/* Persistent warp-specialised tcgen05 kernel, 128 x 256 tiles.
+ * Needs FLOAT16/BFLOAT16, K % 8 == 0, N % 8 == 0, 16-byte aligned pointers. */
+AOTK_API int aotk_gemm_tc(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
+                 int dtype, void* stream);
+
+/* Skinny (decode) kernel: computes C^T = B^T A^T on tcgen05 with the weight
+ * streamed by TMA and K split across a thread-block cluster whose partial sums
+ * are reduced through distributed shared memory.  Same preconditions as
+ * aotk_gemm_tc plus M <= 128. */
+AOTK_API int aotk_gemm_skinny(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
+                     int dtype, void* stream);
+
+/* Watchdog word of the tcgen05 kernels on `device`: a bit mask of pipeline
+ * waits that gave up after their time limit (0 = healthy).  Synchronises the
+ * device.  clear != 0 resets it to 0 after reading. */
+AOTK_API int aotk_watchdog_status(int device, uint32_t* status, int clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AOTK_H_ */

@@ -1,0 +1,144 @@
+"""ctypes binding of the C ABI in ``include/aotk.h`` (``libaotk.so``).
+
+This is the binding a non-torch host would write; the parity tests call the
+kernels through it so that what they check is the C ABI itself.  Every
+wrapper takes device pointers as integers (or torch tensors, converted with
+``data_ptr()``) and a stream handle (default: torch's current stream when
+torch is importable, else the legacy default stream), and raises
+``AotkError`` with ``aotk_last_error()`` on a non-zero status.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libaotk.so"
+
+FLOAT32, FLOAT16, BFLOAT16 = 0, 1, 2
+OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_CUDA, ERR_DEVICE = 0, 1, 2, 3, 4
+
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+_ptr = ctypes.c_void_p
+
+# name -> argument types (all return int except aotk_last_error)
+SIGNATURES: dict[str, list] = {
+    "aotk_version": [],
+    "aotk_silu_forward": [_ptr, _ptr, _i64, _int, _ptr],
+    "aotk_relu_forward": [_ptr, _ptr, _i64, _int, _ptr],
+    "aotk_silu_mul_forward": [_ptr, _i64, _ptr, _i64, _ptr, _i64, _i64, _i64, _int, _ptr],
+    "aotk_rmsnorm_forward": [_ptr, _ptr, _ptr, _i64, _i64, ctypes.c_double, _int, _ptr],
+    "aotk_gemm_opt": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
+    "aotk_gemm": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
+    "aotk_gemm_tc": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
+    "aotk_gemm_skinny": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
+    "aotk_watchdog_status": [_int, ctypes.POINTER(ctypes.c_uint32), _int],
+}
+
+
+class AotkError(RuntimeError):
+    def __init__(self, fn: str, status: int, message: str):
+        super().__init__(f"{fn} returned {status}: {message}")
+        self.status = status
+
+
+_lib: ctypes.CDLL | None = None
+
+
+def load(path: str | Path | None = None) -> ctypes.CDLL:
+    """Loads libaotk.so once and declares every entry point's signature."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    lib = ctypes.CDLL(str(path or LIB_PATH))
+    lib.aotk_last_error.restype = ctypes.c_char_p
+    lib.aotk_last_error.argtypes = []
+    for name, argtypes in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = ctypes.c_int
+        fn.argtypes = argtypes
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def dtype_code(dtype) -> int:
+    import torch
+
+    return {torch.float32: FLOAT32, torch.float16: FLOAT16, torch.bfloat16: BFLOAT16}[dtype]
+
+
+def _p(x) -> int | None:
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    return x.data_ptr()
+
+
+def _stream(stream) -> int | None:
+    if stream is not None:
+        return int(stream)
+    try:
+        import torch
+
+        if torch.cuda.is_available():
+            return torch.cuda.current_stream().cuda_stream
+    except ImportError:
+        pass
+    return None
+
+
+def _call(name: str, *args) -> None:
+    lib = load()
+    status = getattr(lib, name)(*args)
+    if status != OK:
+        raise AotkError(name, status, lib.aotk_last_error().decode())
+
+
+def silu_forward(out, x, n: int, dtype: int, stream=None) -> None:
+    _call("aotk_silu_forward", _p(out), _p(x), n, dtype, _stream(stream))
+
+
+def relu_forward(out, x, n: int, dtype: int, stream=None) -> None:
+    _call("aotk_relu_forward", _p(out), _p(x), n, dtype, _stream(stream))
+
+
+def silu_mul_forward(out, out_stride, gate, gate_stride, up, up_stride, rows, cols, dtype,
+                     stream=None) -> None:
+    _call("aotk_silu_mul_forward", _p(out), out_stride, _p(gate), gate_stride, _p(up), up_stride,
+          rows, cols, dtype, _stream(stream))
+
+
+def rmsnorm_forward(out, x, weight, rows: int, cols: int, eps: float, dtype: int,
+                    stream=None) -> None:
+    _call("aotk_rmsnorm_forward", _p(out), _p(x), _p(weight), rows, cols, eps, dtype,
+          _stream(stream))
+
+
+def _gemm(name, c, a, b, M, N, K, dtype, stream) -> None:
+    _call(name, _p(c), _p(a), _p(b), M, N, K, dtype, _stream(stream))
+
+
+def gemm_opt(c, a, b, M, N, K, dtype, stream=None) -> None:
+    _gemm("aotk_gemm_opt", c, a, b, M, N, K, dtype, stream)
+
+
+def gemm(c, a, b, M, N, K, dtype, stream=None) -> None:
+    _gemm("aotk_gemm", c, a, b, M, N, K, dtype, stream)
+
+
+def gemm_tc(c, a, b, M, N, K, dtype, stream=None) -> None:
+    _gemm("aotk_gemm_tc", c, a, b, M, N, K, dtype, stream)
+
+
+def gemm_skinny(c, a, b, M, N, K, dtype, stream=None) -> None:
+    _gemm("aotk_gemm_skinny", c, a, b, M, N, K, dtype, stream)
+
+
+def watchdog_status(device: int = 0, clear: bool = True) -> int:
+    """Bit mask of tensor-core pipeline waits that timed out (0 = healthy)."""
+    v = ctypes.c_uint32(0)
+    _call("aotk_watchdog_status", device, ctypes.byref(v), 1 if clear else 0)
+    return v.value

@@ -1,0 +1,136 @@
+// C-ABI GEMM entry points and the path selection of aotk_gemm_opt.
+//
+// Path choice (all fp32 accumulation, one rounding per output):
+//   16-bit, TMA-addressable, M <= 128  -> skinny swap-AB split-K kernel
+//                                          (decode; HBM-bound on the weight)
+//   16-bit, TMA-addressable, M > 128   -> persistent tcgen05 kernel
+//   anything else                       -> SIMT kernel
+// The reference routes in its Python wrapper instead: fp16/bf16 with
+// K % 16 == 0 to gemm_opt, everything else to the naive tier
+// (aot_kernel/gemm.py:39-42).
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "common.h"
+#include "gemm_internal.h"
+
+namespace aotk {
+
+namespace {
+
+struct SmemKey {
+  const void* kernel;
+  int device;
+};
+
+std::mutex g_smem_mu;
+SmemKey g_smem_done[256];
+int g_smem_count = 0;
+
+int validate_common(const char* who, const void* c, const void* a, const void* b, int64_t M,
+                    int64_t N, int64_t K, int dtype) {
+  if (M < 0 || N < 0 || K < 0)
+    return fail(AOTK_ERR_INVALID_ARGUMENT, "%s: negative size (M=%lld N=%lld K=%lld)", who,
+                (long long)M, (long long)N, (long long)K);
+  if (!valid_dtype(dtype)) return fail(AOTK_ERR_UNSUPPORTED, "%s: unsupported dtype %d", who, dtype);
+  if (M > 0 && N > 0 && (!c || (K > 0 && (!a || !b))))
+    return fail(AOTK_ERR_INVALID_ARGUMENT, "%s: null pointer", who);
+  return AOTK_OK;
+}
+
+// C = 0 when K == 0 (an empty sum), matching `a @ b` for an empty inner dim.
+int zero_output(void* c, int64_t M, int64_t N, int dtype, void* stream) {
+  cudaError_t e = cudaMemsetAsync(c, 0, (size_t)(M * N * elem_size(dtype)),
+                                  static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(AOTK_ERR_CUDA, "gemm: cudaMemsetAsync: %s", cudaGetErrorString(e));
+  return AOTK_OK;
+}
+
+}  // namespace
+
+int ensure_dynamic_smem(const void* kernel, int bytes, const DeviceInfo& info) {
+  std::lock_guard<std::mutex> lock(g_smem_mu);
+  for (int i = 0; i < g_smem_count; ++i) {
+    if (g_smem_done[i].kernel == kernel && g_smem_done[i].device == info.device) return AOTK_OK;
+  }
+  if (bytes > info.max_smem_optin)
+    return fail(AOTK_ERR_DEVICE, "kernel needs %d bytes of shared memory, device allows %d", bytes,
+                info.max_smem_optin);
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess)
+    return fail(AOTK_ERR_CUDA, "cudaFuncSetAttribute(smem=%d): %s", bytes, cudaGetErrorString(e));
+  if (g_smem_count < 256) g_smem_done[g_smem_count++] = SmemKey{kernel, info.device};
+  return AOTK_OK;
+}
+
+bool tc_eligible(const void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
+                 int dtype) {
+  if (dtype != AOTK_FLOAT16 && dtype != AOTK_BFLOAT16) return false;
+  if (K % 8 != 0 || N % 8 != 0) return false;
+  if (M >= (1LL << 31) || N >= (1LL << 31) || K >= (1LL << 31)) return false;
+  return aligned16(a) && aligned16(b) && aligned16(c);
+}
+
+int check_tc_preconditions(const char* who, const void* c, const void* a, const void* b, int64_t M,
+                           int64_t N, int64_t K, int dtype) {
+  if (int st = validate_common(who, c, a, b, M, N, K, dtype)) return st;
+  if (M == 0 || N == 0 || K == 0)
+    return fail(AOTK_ERR_INVALID_ARGUMENT, "%s: empty problem (M=%lld N=%lld K=%lld)", who,
+                (long long)M, (long long)N, (long long)K);
+  if (!tc_eligible(c, a, b, M, N, K, dtype))
+    return fail(AOTK_ERR_UNSUPPORTED,
+                "%s: needs fp16/bf16, K %% 8 == 0, N %% 8 == 0 and 16-byte aligned pointers "
+                "(dtype=%d M=%lld N=%lld K=%lld)",
+                who, dtype, (long long)M, (long long)N, (long long)K);
+  return AOTK_OK;
+}
+
+}  // namespace aotk
+
+extern "C" int aotk_gemm_opt(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
+                             int dtype, void* stream) {
+  using namespace aotk;
+  if (int st = validate_common("aotk_gemm_opt", c, a, b, M, N, K, dtype)) return st;
+  if (dtype == AOTK_FLOAT32)
+    return fail(AOTK_ERR_UNSUPPORTED, "aotk_gemm_opt: tensor-core path supports fp16/bf16 only");
+  if (M == 0 || N == 0) return AOTK_OK;
+  if (K == 0) return zero_output(c, M, N, dtype, stream);
+  if (tc_eligible(c, a, b, M, N, K, dtype)) {
+    if (M <= kSkinnyMaxM) return gemm_skinny(c, a, b, M, N, K, dtype, stream);
+    return gemm_tc(c, a, b, M, N, K, dtype, stream);
+  }
+  return gemm_simt(c, a, b, M, N, K, dtype, stream);
+}
+
+extern "C" int aotk_gemm(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
+                         int dtype, void* stream) {
+  using namespace aotk;
+  if (int st = validate_common("aotk_gemm", c, a, b, M, N, K, dtype)) return st;
+  if (M == 0 || N == 0) return AOTK_OK;
+  return gemm_simt(c, a, b, M, N, K, dtype, stream);
+}
+
+extern "C" int aotk_gemm_tc(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
+                            int dtype, void* stream) {
+  return aotk::gemm_tc(c, a, b, M, N, K, dtype, stream);
+}
+
+extern "C" int aotk_gemm_skinny(void* c, const void* a, const void* b, int64_t M, int64_t N,
+                                int64_t K, int dtype, void* stream) {
+  return aotk::gemm_skinny(c, a, b, M, N, K, dtype, stream);
+}
+
+extern "C" int aotk_watchdog_status(int device, uint32_t* status, int clear) {
+  using namespace aotk;
+  if (!status) return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_watchdog_status: null pointer");
+  int prev = 0;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e == cudaSuccess) e = cudaSetDevice(device);
+  if (e != cudaSuccess) return fail(AOTK_ERR_CUDA, "aotk_watchdog_status: %s", cudaGetErrorString(e));
+  *status = 0;
+  int st = tc_watchdog(status, clear != 0);
+  if (st == AOTK_OK) st = skinny_watchdog(status, clear != 0);
+  cudaSetDevice(prev);
+  return st;
+}

@@ -1,0 +1,37 @@
+// Internal interface between the GEMM kernels and the C-ABI dispatcher.
+#pragma once
+
+#include <cstdint>
+
+#include "common.h"
+
+namespace aotk {
+
+// Persistent tcgen05 kernel (gemm_tc.cu).
+int gemm_tc(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K, int dtype,
+            void* stream);
+
+// Swap-AB split-K tcgen05 kernel for M <= kSkinnyMaxM (gemm_skinny.cu).
+constexpr int64_t kSkinnyMaxM = 128;
+int gemm_skinny(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K, int dtype,
+                void* stream);
+
+// SIMT kernel for every dtype and shape (gemm_simt.cu).
+int gemm_simt(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K, int dtype,
+              void* stream);
+
+// Watchdog words of the tensor-core kernels (OR-ed into *status).
+int tc_watchdog(uint32_t* status, bool clear);
+int skinny_watchdog(uint32_t* status, bool clear);
+
+// Raises the dynamic shared-memory limit of `kernel` to `bytes` once per device.
+int ensure_dynamic_smem(const void* kernel, int bytes, const DeviceInfo& info);
+
+// Preconditions shared by the TMA-fed kernels: 16-bit dtype, K % 8 == 0,
+// N % 8 == 0 (16-byte row strides), 16-byte aligned bases, 32-bit extents.
+bool tc_eligible(const void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
+                 int dtype);
+int check_tc_preconditions(const char* who, const void* c, const void* a, const void* b, int64_t M,
+                           int64_t N, int64_t K, int dtype);
+
+}  // namespace aotk

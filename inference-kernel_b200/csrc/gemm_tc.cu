@@ -1,0 +1,337 @@
+// Persistent, warp-specialised tcgen05 GEMM: C[M,N] = A[M,K] * B[K,N].
+//
+// One CTA per SM walks output tiles of 128 x BN (grouped raster for L2
+// reuse).  Six warps split the work:
+//   warp 0      TMA producer: per 64-wide K block, one 128 x 64 box of A
+//               (K-major) and BN/64 boxes of 64 x 64 of B (N-major), all
+//               128-byte swizzled, into a STAGES-deep shared-memory ring
+//               guarded by full/empty mbarriers;
+//   warp 1      MMA issuer: allocates 2 * BN TMEM columns (two fp32
+//               accumulators), issues tcgen05.mma M=128 N=BN K=16 with A
+//               K-major and B MN-major straight from the swizzled stages (no
+//               transpose pass), and commits each stage back to the
+//               producer and each finished accumulator to the epilogue;
+//   warps 2-5   epilogue: tcgen05.ld of their 32-lane TMEM quarter, fp32 ->
+//               16-bit, swizzled 32 x 64 staging boxes, TMA stores (double
+//               buffered per warp).  The accumulator is handed back as soon
+//               as it is read, so the next tile's main loop overlaps this
+//               tile's stores.
+// Every pipeline wait is bounded (sm100.cuh): on a timeout the kernel records
+// a watchdog bit, lets the other roles drop out, drains its in-flight copies
+// and frees TMEM before returning.
+//
+// Replaces the reference's WMMA/cp.async kernel gemm_wmma_pipe_kernel
+// (aot_kernel/csrc/gemm/gemm_opt.cu:30-195): 128 x 128 x 32 tiles, 2 stages,
+// one CTA per tile, fp32 epilogue through shared memory.
+#include "common.h"
+#include "gemm_internal.h"
+#include "sm100.cuh"
+#include "tmap.h"
+#include "vec.cuh"
+
+namespace aotk {
+namespace {
+
+using namespace sm100;
+
+__device__ unsigned g_tc_watchdog;
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // one 128-byte swizzle row of 16-bit elements
+constexpr int kUmmaK = 16;
+constexpr int kThreads = 192;
+constexpr int kGroupM = 16;  // M tiles per raster group
+
+enum : unsigned { kWdProducer = 1u, kWdMma = 2u, kWdEpilogue = 4u };
+
+template <int BN, int STAGES>
+struct TcLayout {
+  static constexpr uint32_t kABytes = kBM * kBK * 2;
+  static constexpr uint32_t kBBox = kBK * 128;  // one 64 (N) x 64 (K) box
+  static constexpr uint32_t kBBytes = (BN / 64) * kBBox;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kCBuf = 32 * 128;  // 32 rows x 64 columns x 2 bytes
+  static constexpr uint32_t kOffA = 0;
+  static constexpr uint32_t kOffB = kOffA + STAGES * kABytes;
+  static constexpr uint32_t kOffC = kOffB + STAGES * kBBytes;
+  static constexpr uint32_t kOffBar = kOffC + 4 * 2 * kCBuf;
+  static constexpr uint32_t kNumBars = 2 * STAGES + 5;  // full, empty, tmem full/empty x2, drain
+  static constexpr uint32_t kOffMisc = kOffBar + kNumBars * 8;
+  static constexpr uint32_t kBytes = kOffMisc + 16;
+  static constexpr uint32_t kAlloc = kBytes + 1024;  // base is rounded up to 1 KB
+  static constexpr uint32_t kTmemCols = 2 * BN;
+  static_assert(BN % 64 == 0 && BN <= 256, "BN must be 64..256 in steps of 64");
+  static_assert(kTmemCols <= 512, "two accumulators must fit in TMEM");
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& mb, int& nb) {
+  const int per_group = kGroupM * tiles_n;
+  const int g = tile / per_group;
+  const int first_m = g * kGroupM;
+  const int gm = min(tiles_m - first_m, kGroupM);
+  const int local = tile - g * per_group;
+  mb = first_m + local % gm;
+  nb = local / gm;
+}
+
+template <typename T, int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, int M, int N, int K, uint32_t idesc) {
+  using L = TcLayout<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_addr(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw);
+  const uint32_t sA = base + L::kOffA;
+  const uint32_t sB = base + L::kOffB;
+  const uint32_t sC = base + L::kOffC;
+  const uint32_t bar0 = base + L::kOffBar;
+  const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
+  unsigned* wd = &g_tc_watchdog;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tiles_m = (M + kBM - 1) / kBM;
+  const int tiles_n = (N + BN - 1) / BN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int kblocks = (K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_addr(tmem_slot), L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, tiles_m, tiles_n, mb, nb);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, wd, kWdProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full_bar(stage);
+          mbar_arrive_expect_tx(fb, L::kStageBytes);
+          tma_load_2d(sA + stage * L::kABytes, &tmA, kb * kBK, mb * kBM, fb);
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j) {
+            tma_load_2d(sB + stage * L::kBBytes + j * L::kBBox, &tmB, nb * BN + j * 64, kb * kBK, fb);
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Loads already issued must land before this CTA may exit.
+      int s = stage;
+      uint32_t p = phase;
+      for (int i = 0; i < STAGES && i < issued; ++i) {
+        if (--s < 0) {
+          s = STAGES - 1;
+          p ^= 1u;
+        }
+        mbar_drain(full_bar(s), p);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait_bounded(tempty_bar(acc), acc_phase ^ 1u, abort_flag, wd, kWdMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_bounded(full_bar(stage), phase, abort_flag, wd, kWdMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = sA + stage * L::kABytes;
+          const uint32_t b0 = sB + stage * L::kBBytes;
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            // A: K-major, advance 16 elements (32 B) inside the swizzle row.
+            // B: MN-major, advance 16 K rows (2 atoms of 8 rows x 128 B).
+            const uint64_t ad = sdesc_sw128(a0 + k * kUmmaK * 2, 16, 1024);
+            const uint64_t bd = sdesc_sw128(b0 + k * kUmmaK * 128, L::kBBox, 1024);
+            umma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0);
+          }
+          umma_commit(empty_bar(stage));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(tfull_bar(acc));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // Every MMA issued by this thread completes before TMEM is released.
+      umma_commit(drain_bar);
+      mbar_drain(drain_bar, 0);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const uint32_t cbuf = sC + (warp - 2) * 2 * L::kCBuf;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int nstore = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int mb, nb;
+      tile_coords(tile, tiles_m, tiles_n, mb, nb);
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait_bounded(tfull_bar(acc), acc_phase, abort_flag, wd, kWdEpilogue);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t trow = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                            static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 64; ++c) {
+        uint32_t r[64];
+        tmem_ld_32x32b_x32(trow + c * 64, r);
+        tmem_ld_32x32b_x32(trow + c * 64 + 32, r + 32);
+        tmem_wait_ld();
+        if (c == BN / 64 - 1) {
+          // Accumulator fully read: hand it back to the MMA warp.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(tempty_bar(acc));
+        }
+        const int store_x = nb * BN + c * 64;
+        const int store_y = mb * kBM + q * 32;
+        if (store_x >= N || store_y >= M) continue;  // box entirely outside C
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          pk[i] = Elem<T>::pack2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+        const uint32_t buf = cbuf + (nstore & 1) * L::kCBuf;
+        if (nstore >= 2 && lane == 0) bulk_wait_read<1>();
+        __syncwarp();
+        // Row `lane` of the 32 x 64 box, 16-byte chunk j stored at j ^ (row % 8)
+        // (the 128-byte swizzle the store's tensor map expects).
+        const uint32_t row = buf + lane * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          st_shared_v4(row + ((j ^ (lane & 7)) << 4), pk[4 * j], pk[4 * j + 1], pk[4 * j + 2],
+                       pk[4 * j + 3]);
+        }
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, buf, store_x, store_y);
+          bulk_commit();
+        }
+        ++nstore;
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::kTmemCols);
+  }
+}
+
+template <typename T, int BN, int STAGES>
+int launch_tc(void* c, const void* a, const void* b, int M, int N, int K, bool bf16,
+              cudaStream_t stream, const DeviceInfo& info) {
+  using L = TcLayout<BN, STAGES>;
+  auto kernel = gemm_tc_kernel<T, BN, STAGES>;
+  if (int st = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), L::kAlloc, info)) return st;
+  CUtensorMap ta, tb, tc;
+  if (int st = make_tmap_2d_16bit(&ta, a, bf16, M, K, K, kBK, kBM)) return st;
+  if (int st = make_tmap_2d_16bit(&tb, b, bf16, K, N, N, 64, kBK)) return st;
+  if (int st = make_tmap_2d_16bit(&tc, c, bf16, M, N, N, 64, 32)) return st;
+  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+  const int grid = tiles < info.sm_count ? tiles : info.sm_count;
+  const uint32_t idesc = idesc_f16(bf16, kBM, BN, /*a_mn_major=*/false, /*b_mn_major=*/true);
+  kernel<<<grid, kThreads, L::kAlloc, stream>>>(ta, tb, tc, M, N, K, idesc);
+  return check_launch("tcgen05 gemm");
+}
+
+}  // namespace
+
+int gemm_tc(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K, int dtype,
+            void* stream) {
+  DeviceInfo info;
+  if (int st = current_device_info(&info)) return st;
+  if (int st = require_sm100(info)) return st;
+  if (int st = check_tc_preconditions("aotk_gemm_tc", c, a, b, M, N, K, dtype)) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int m = (int)M, n = (int)N, k = (int)K;
+  if (dtype == AOTK_BFLOAT16) return launch_tc<__nv_bfloat16, 256, 4>(c, a, b, m, n, k, true, s, info);
+  return launch_tc<__half, 256, 4>(c, a, b, m, n, k, false, s, info);
+}
+
+int tc_watchdog(uint32_t* status, bool clear) {
+  unsigned v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_tc_watchdog, sizeof(v));
+  if (e != cudaSuccess) return fail(AOTK_ERR_CUDA, "watchdog read: %s", cudaGetErrorString(e));
+  if (clear) {
+    const unsigned zero = 0;
+    e = cudaMemcpyToSymbol(g_tc_watchdog, &zero, sizeof(zero));
+    if (e != cudaSuccess) return fail(AOTK_ERR_CUDA, "watchdog clear: %s", cudaGetErrorString(e));
+  }
+  *status |= v;
+  return AOTK_OK;
+}
+
+}  // namespace aotk

@@ -1,0 +1,195 @@
+// torch operator library `aot_kernel`: the same schemas as the reference's
+// registration (aot_kernel/csrc/registration.cc:10-25) plus silu_mul_forward.
+// Each kernel checks its tensors, pins the device, and calls the C ABI of
+// libaotk (include/aotk.h) on the current torch stream.  Unlike the
+// reference, launches go to at::cuda::getCurrentCUDAStream() under a device
+// guard rather than to the legacy default stream, and every launch status is
+// checked.
+#include <Python.h>
+#include <ATen/ATen.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/library.h>
+
+#include "aotk.h"
+
+namespace {
+
+int aotk_dtype(const at::Tensor& t, const char* op) {
+  switch (t.scalar_type()) {
+    case at::ScalarType::Float: return AOTK_FLOAT32;
+    case at::ScalarType::Half: return AOTK_FLOAT16;
+    case at::ScalarType::BFloat16: return AOTK_BFLOAT16;
+    default: TORCH_CHECK(false, "[", op, "] unsupported dtype: ", t.scalar_type());
+  }
+  return -1;
+}
+
+void* current_stream(const at::Tensor& t) {
+  return at::cuda::getCurrentCUDAStream(t.device().index()).stream();
+}
+
+void check_status(int status, const char* op) {
+  TORCH_CHECK(status == AOTK_OK, "[", op, "] ", aotk_last_error());
+}
+
+void check_cuda(const at::Tensor& t, const char* op, const char* name) {
+  TORCH_CHECK(t.is_cuda(), "[", op, "] ", name, " must be a CUDA tensor, got ", t.device());
+}
+
+void check_same(const at::Tensor& a, const at::Tensor& b, const char* op, const char* an,
+                const char* bn) {
+  TORCH_CHECK(a.device() == b.device(), "[", op, "] ", an, " and ", bn,
+              " are not on the same device: ", a.device(), " vs ", b.device());
+  TORCH_CHECK(a.scalar_type() == b.scalar_type(), "[", op, "] ", an, " and ", bn,
+              " have different dtypes: ", a.scalar_type(), " vs ", b.scalar_type());
+}
+
+void check_out_like(const at::Tensor& out, const at::Tensor& x, const char* op) {
+  check_cuda(out, op, "out");
+  check_same(out, x, op, "out", "x");
+  TORCH_CHECK(out.is_contiguous(), "[", op, "] out is not contiguous");
+  TORCH_CHECK(out.sizes() == x.sizes(), "[", op, "] out shape ", out.sizes(),
+              " does not match input shape ", x.sizes());
+}
+
+void relu_forward(at::Tensor out, at::Tensor x) {
+  const char* op = "relu_forward";
+  check_cuda(x, op, "x");
+  TORCH_CHECK(x.is_contiguous(), "[", op, "] x must be contiguous");
+  check_out_like(out, x, op);
+  c10::cuda::CUDAGuard guard(x.device());
+  check_status(aotk_relu_forward(out.data_ptr(), x.data_ptr(), x.numel(), aotk_dtype(x, op),
+                                 current_stream(x)),
+               op);
+}
+
+void silu_forward(at::Tensor out, at::Tensor x) {
+  const char* op = "silu_forward";
+  check_cuda(x, op, "x");
+  TORCH_CHECK(x.is_contiguous(), "[", op, "] x must be contiguous");
+  check_out_like(out, x, op);
+  c10::cuda::CUDAGuard guard(x.device());
+  check_status(aotk_silu_forward(out.data_ptr(), x.data_ptr(), x.numel(), aotk_dtype(x, op),
+                                 current_stream(x)),
+               op);
+}
+
+// gate / up / out: same shape; each either contiguous or a 2-D view whose
+// rows are contiguous (e.g. the two column halves of a [rows, 2*cols] tensor).
+int64_t row_stride(const at::Tensor& t, const char* op, const char* name) {
+  if (t.is_contiguous()) return t.dim() == 0 ? 1 : t.size(-1);
+  TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1 && t.stride(0) >= t.size(1), "[", op, "] ", name,
+              " must be contiguous or a 2-D view with contiguous rows");
+  return t.stride(0);
+}
+
+void silu_mul_forward(at::Tensor out, at::Tensor gate, at::Tensor up) {
+  const char* op = "silu_mul_forward";
+  check_cuda(gate, op, "gate");
+  check_cuda(up, op, "up");
+  check_cuda(out, op, "out");
+  check_same(gate, up, op, "gate", "up");
+  check_same(out, gate, op, "out", "gate");
+  TORCH_CHECK(gate.sizes() == up.sizes() && out.sizes() == gate.sizes(), "[", op,
+              "] shape mismatch: gate ", gate.sizes(), " up ", up.sizes(), " out ", out.sizes());
+  const int64_t cols = gate.dim() == 0 ? 1 : gate.size(-1);
+  const int64_t rows = cols == 0 ? 0 : gate.numel() / cols;
+  const int64_t gs = row_stride(gate, op, "gate");
+  const int64_t us = row_stride(up, op, "up");
+  const int64_t os = row_stride(out, op, "out");
+  c10::cuda::CUDAGuard guard(gate.device());
+  check_status(aotk_silu_mul_forward(out.data_ptr(), os, gate.data_ptr(), gs, up.data_ptr(), us,
+                                     rows, cols, aotk_dtype(gate, op), current_stream(gate)),
+               op);
+}
+
+void rmsnorm_forward(at::Tensor out, at::Tensor x, at::Tensor weight, double eps) {
+  const char* op = "rmsnorm";
+  check_cuda(x, op, "x");
+  check_cuda(weight, op, "weight");
+  check_same(x, weight, op, "x", "weight");
+  TORCH_CHECK(x.is_contiguous(), "[", op, "] x is not contiguous");
+  TORCH_CHECK(weight.is_contiguous(), "[", op, "] weight is not contiguous");
+  TORCH_CHECK(weight.dim() == 1, "[", op, "] dim of weight is not 1, got ", weight.dim());
+  TORCH_CHECK(x.dim() >= 1 && weight.size(0) == x.size(-1), "[", op,
+              "] weight length must equal x.size(-1), got weight_length=", weight.size(0),
+              " x.size(-1)=", x.dim() >= 1 ? x.size(-1) : 0);
+  check_out_like(out, x, op);
+  if (x.numel() == 0) return;
+  const int64_t cols = x.size(-1);
+  const int64_t rows = x.numel() / cols;
+  c10::cuda::CUDAGuard guard(x.device());
+  check_status(aotk_rmsnorm_forward(out.data_ptr(), x.data_ptr(), weight.data_ptr(), rows, cols,
+                                    eps, aotk_dtype(x, op), current_stream(x)),
+               op);
+}
+
+struct GemmArgs {
+  int64_t M, N, K;
+  int dtype;
+};
+
+GemmArgs check_gemm(const at::Tensor& out, const at::Tensor& a, const at::Tensor& b,
+                    const char* op) {
+  check_cuda(a, op, "a");
+  check_cuda(b, op, "b");
+  check_cuda(out, op, "out");
+  check_same(a, b, op, "a", "b");
+  check_same(out, a, op, "out", "a");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2, "[", op, "] expects 2D tensors, got a.dim=", a.dim(),
+              " b.dim=", b.dim());
+  TORCH_CHECK(a.size(1) == b.size(0), "[", op, "] inner dims mismatch: ", a.size(1), " vs ",
+              b.size(0));
+  TORCH_CHECK(a.is_contiguous() && b.is_contiguous() && out.is_contiguous(), "[", op,
+              "] tensors must be contiguous");
+  TORCH_CHECK(out.dim() == 2 && out.size(0) == a.size(0) && out.size(1) == b.size(1), "[", op,
+              "] out must be [", a.size(0), ", ", b.size(1), "], got ", out.sizes());
+  return GemmArgs{a.size(0), b.size(1), a.size(1), aotk_dtype(a, op)};
+}
+
+void gemm(at::Tensor out, at::Tensor a, at::Tensor b) {
+  const char* op = "gemm";
+  const GemmArgs g = check_gemm(out, a, b, op);
+  c10::cuda::CUDAGuard guard(a.device());
+  check_status(aotk_gemm(out.data_ptr(), a.data_ptr(), b.data_ptr(), g.M, g.N, g.K, g.dtype,
+                         current_stream(a)),
+               op);
+}
+
+void gemm_opt(at::Tensor out, at::Tensor a, at::Tensor b) {
+  const char* op = "gemm_opt";
+  const GemmArgs g = check_gemm(out, a, b, op);
+  c10::cuda::CUDAGuard guard(a.device());
+  check_status(aotk_gemm_opt(out.data_ptr(), a.data_ptr(), b.data_ptr(), g.M, g.N, g.K, g.dtype,
+                             current_stream(a)),
+               op);
+}
+
+}  // namespace
+
+TORCH_LIBRARY(aot_kernel, m) {
+  m.def("relu_forward(Tensor! out, Tensor x) -> ()");
+  m.impl("relu_forward", c10::kCUDA, &relu_forward);
+
+  m.def("silu_forward(Tensor! out, Tensor x) -> ()");
+  m.impl("silu_forward", c10::kCUDA, &silu_forward);
+
+  m.def("silu_mul_forward(Tensor! out, Tensor gate, Tensor up) -> ()");
+  m.impl("silu_mul_forward", c10::kCUDA, &silu_mul_forward);
+
+  m.def("rmsnorm_forward(Tensor! out, Tensor x, Tensor weight, float eps) -> ()");
+  m.impl("rmsnorm_forward", c10::kCUDA, &rmsnorm_forward);
+
+  m.def("gemm(Tensor! out, Tensor a, Tensor b) -> ()");
+  m.impl("gemm", c10::kCUDA, &gemm);
+
+  m.def("gemm_opt(Tensor! out, Tensor a, Tensor b) -> ()");
+  m.impl("gemm_opt", c10::kCUDA, &gemm_opt);
+}
+
+// `import aot_kernel._C` runs the static registration above; the module itself is empty.
+PyMODINIT_FUNC PyInit__C(void) {
+  static struct PyModuleDef module = {PyModuleDef_HEAD_INIT, "_C", nullptr, 0, nullptr};
+  return PyModule_Create(&module);
+}

@@ -1,0 +1,59 @@
+#include "tmap.h"
+
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "common.h"
+
+namespace aotk {
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int encoder(EncodeTiledFn* fn) {
+  std::call_once(g_encode_once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      g_encode = reinterpret_cast<EncodeTiledFn>(p);
+    }
+  });
+  if (!g_encode) return fail(AOTK_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  *fn = g_encode;
+  return AOTK_OK;
+}
+
+}  // namespace
+
+int make_tmap_2d_16bit(CUtensorMap* map, const void* base, bool bf16, uint64_t rows, uint64_t cols,
+                       uint64_t ld, uint32_t box_cols, uint32_t box_rows) {
+  EncodeTiledFn fn;
+  if (int st = encoder(&fn)) return st;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {ld * 2};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estrides[2] = {1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                  const_cast<void*>(base), dims, strides, box, estrides,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    return fail(AOTK_ERR_CUDA,
+                "cuTensorMapEncodeTiled failed (%d) for [%llu x %llu] ld=%llu box=%ux%u", (int)r,
+                (unsigned long long)rows, (unsigned long long)cols, (unsigned long long)ld,
+                box_cols, box_rows);
+  }
+  return AOTK_OK;
+}
+
+}  // namespace aotk
