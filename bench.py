@@ -1,0 +1,493 @@
+#!/usr/bin/env python
+"""Benchmark of the dense-linear inference path on B200.
+
+Headline (one JSON line on rank 0): bf16 GEMM TFLOP/s on the square
+M = N = K = 8192 problem (fp32 accumulation, bf16 output) through the
+``aot_kernel`` public API.  A step is one GEMM over operands already resident
+in HBM; at N GPUs every rank runs its own GEMM (independent replicas, weak
+scaling) and ``value`` is the sum over ranks.  The same line carries:
+
+* ``roofline``  - the GEMM kernel's achieved TFLOP/s (2*M*N*K / mean CUDA-event
+  duration of its launches) against the measured bf16 peak;
+* ``e2e``       - the same metric through the public API with pinned host
+  buffers: host->device copy of A and B, the GEMM, device->host copy of C;
+* ``cpu_baseline`` - the oracle's CPU GEMM (numpy, all host threads) on a
+  bounded row sample of the same problem (rank 0, N = 1);
+* ``kernels``   - the remaining workloads of the path at their configured sizes:
+  the square sweep, the Llama-3-8B linear layers from decode to prefill,
+  rms_norm, silu and silu(gate)*up, each with its roofline fraction (N = 1);
+* ``tp_mlp``    - tokens/s of the Llama-3-70B MLP block (4096 tokens,
+  hidden 8192, intermediate 28672) tensor-parallel over the N ranks with one
+  NCCL all-reduce (the multi-GPU path; strong scaling in tokens).
+
+``--impl reference`` times the reference's CPU path (the oracle port of
+``ref.gemm``, all host threads) on the same metric instead; under torchrun
+only rank 0 runs it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+for _p in (REPO, REPO / "inference-kernel_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+HEADLINE = (8192, 8192, 8192)
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-kernels", action="store_true", help="skip the per-workload table")
+    ap.add_argument("--no-tp", action="store_true", help="skip the tensor-parallel MLP block")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--tp-chunks", type=int, default=1)
+    return ap.parse_args()
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return {k: float(d[k]) for k in FALLBACK_PEAKS}, "measured"
+        except (KeyError, ValueError):
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples every 200 ms while active."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self, devices: set[int] | None = None) -> dict:
+        self.file.flush()
+        self.file.seek(0)
+        rows = list(csv.reader(io.StringIO(self.file.read())))
+        os.unlink(self.file.name)
+        mhz, max_mhz, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            if len(r) < 9:
+                continue
+            try:
+                idx, sm, smax, power = int(r[0]), float(r[1]), float(r[2]), float(r[3])
+            except ValueError:
+                continue
+            if devices is not None and idx not in devices:
+                continue
+            max_mhz = max(max_mhz, smax)
+            if power > 300.0 or sm > 1000.0:  # under load
+                mhz.append(sm)
+            for name, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": max_mhz or None,
+                "reasons": sorted(reasons), "samples_under_load": len(mhz)}
+
+
+# ---------------------------------------------------------------- timing helpers
+
+def per_launch_ms(fn, iters: int, warmup: int, flush=None) -> list[float]:
+    """CUDA-event duration of each of `iters` launches of fn() on the current stream."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        if flush is not None:
+            flush()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        times.append((s, e))
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in times]
+
+
+def make_flush():
+    import torch
+
+    buf = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
+
+    def flush():
+        buf.fill_(1.0)
+
+    return flush
+
+
+# ---------------------------------------------------------------- workloads
+
+def rand_bf16(shape, seed: int, std: float = 1.0, mean: float = 0.0):
+    import torch
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    x = torch.randn(shape, generator=g, device="cuda", dtype=torch.float32)
+    if std != 1.0:
+        x.mul_(std)
+    if mean != 0.0:
+        x.add_(mean)
+    return x.to(torch.bfloat16)
+
+
+def headline_gemm(args, rank: int, world: int, peaks: dict):
+    import torch
+    import torch.distributed as dist
+
+    import aot_kernel
+
+    M, N, K = HEADLINE
+    a = rand_bf16((M, K), 1 + rank)
+    b = rand_bf16((K, N), 2 + rank, std=K ** -0.5)
+    flops = 2.0 * M * N * K
+
+    def step():
+        return aot_kernel.gemm(a, b)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler() as clocks:
+        events = []
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            step()
+            e.record()
+            events.append((s, e))
+        t1.record()
+        torch.cuda.synchronize()
+    total_ms = t0.elapsed_time(t1)
+    launch_ms = statistics.mean(s.elapsed_time(e) for s, e in events)
+    if world > 1:
+        dist.barrier()
+    t = torch.tensor([total_ms, launch_ms], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, launch_ms = t.tolist()
+
+    # end to end through the public API with pinned host buffers
+    a_h = a.cpu().pin_memory()
+    b_h = b.cpu().pin_memory()
+    c_h = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+    a_d, b_d = torch.empty_like(a), torch.empty_like(b)
+
+    def e2e_step():
+        a_d.copy_(a_h, non_blocking=True)
+        b_d.copy_(b_h, non_blocking=True)
+        c = aot_kernel.gemm(a_d, b_d)
+        c_h.copy_(c, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 20))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e.record()
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([s.elapsed_time(e) / e2e_steps], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_ms.item())
+
+    achieved = flops / (launch_ms * 1e-3) / 1e12
+    res = {
+        "value": world * flops * args.steps / (total_ms * 1e-3) / 1e12,
+        "ms_per_step": total_ms / args.steps,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                     "traffic": traffic_per_launch("gemm_tc_8192")},
+        "e2e": {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": a.nbytes + b.nbytes, "d2h_bytes_per_step": M * N * 2,
+                "ms_per_step": e2e_ms},
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+    }
+    del a_h, b_h, c_h
+    return res
+
+
+def traffic_per_launch(key: str):
+    p = REPO / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        return json.loads(p.read_text()).get(key)
+    except ValueError:
+        return None
+
+
+def kernel_table(peaks: dict) -> dict:
+    """Every configured workload of the path, timed per launch with an L2 flush in between."""
+    import torch
+
+    import aot_kernel
+
+    flush = make_flush()
+    out = {}
+    ridge = peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
+
+    def gemm_entry(M, K, N, seed, b_std):
+        a = rand_bf16((M, K), seed)
+        b = rand_bf16((K, N), seed + 1, std=b_std)
+        ms = statistics.mean(per_launch_ms(lambda: aot_kernel.gemm(a, b), 10, 3, flush))
+        flops = 2.0 * M * N * K
+        nbytes = 2.0 * (M * K + K * N + M * N)
+        tf = flops / (ms * 1e-3) / 1e12
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        bound = "tensor" if flops / nbytes >= ridge else "hbm"
+        frac = tf / peaks["bf16_tflops"] if bound == "tensor" else gbs / peaks["hbm_gbs"]
+        return {"ms": round(ms, 5), "tflops": round(tf, 2), "gbs": round(gbs, 1), "bound": bound,
+                "frac": round(frac, 4)}
+
+    for n in (2048, 4096, 8192, 16384):
+        out[f"gemm_{n}^3"] = gemm_entry(n, n, n, 10 + n, n ** -0.5)
+    for K, N in ((4096, 6144), (4096, 28672), (14336, 4096)):
+        for M in (1, 16, 128, 2048, 8192):
+            out[f"linear_M{M}_K{K}_N{N}"] = gemm_entry(M, K, N, M + K + N, 0.02)
+
+    def hbm_entry(fn, nbytes):
+        ms = statistics.mean(per_launch_ms(fn, 20, 3, flush))
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        return {"ms": round(ms, 5), "gbs": round(gbs, 1), "bound": "hbm",
+                "frac": round(gbs / peaks["hbm_gbs"], 4), "bytes": int(nbytes)}
+
+    x = rand_bf16((8192, 4096), 20)
+    w = rand_bf16((4096,), 21, std=0.1, mean=1.0)
+    out["rms_norm_8192x4096"] = hbm_entry(lambda: aot_kernel.rms_norm(x, w), 2 * x.nbytes + w.nbytes)
+    del x
+    g = rand_bf16((8192, 14336), 22, std=2.0)
+    u = rand_bf16((8192, 14336), 23, std=2.0)
+    out["silu_8192x14336"] = hbm_entry(lambda: aot_kernel.silu(g), 2 * g.nbytes)
+    out["silu_mul_8192x14336"] = hbm_entry(lambda: aot_kernel.silu_mul(g, u), 3 * g.nbytes)
+    del g, u
+    torch.cuda.empty_cache()
+    return out
+
+
+def tp_mlp(args, rank: int, world: int, peaks: dict) -> dict:
+    import torch
+    import torch.distributed as dist
+
+    from aot_kernel.tp_mlp import MLPShard, TensorParallelMLP, shard_down, shard_gate_up
+
+    T, H, inter = 4096, 8192, 28672
+    x = rand_bf16((T, H), 30)
+    nw = rand_bf16((H,), 31, std=0.1, mean=1.0)
+    w_gu = rand_bf16((H, 2 * inter), 32, std=0.02)
+    wgu_r = shard_gate_up(w_gu, rank, world)
+    del w_gu
+    w_d = rand_bf16((inter, H), 33, std=0.02)
+    wd_r = shard_down(w_d, rank, world)
+    del w_d
+    torch.cuda.empty_cache()
+    block = TensorParallelMLP(MLPShard(nw, wgu_r, wd_r), eps=1e-6, chunks=args.tp_chunks)
+    for _ in range(max(3, args.warmup)):
+        block(x)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    steps = max(5, min(args.steps, 30))
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        block(x)
+    e.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([s.elapsed_time(e) / steps], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    flops = 2.0 * T * H * 2 * inter + 2.0 * T * inter * H
+    per_gpu_ideal_ms = flops / world / (peaks["bf16_tflops"] * 1e12) * 1e3
+    return {"tokens_per_s": T / (ms * 1e-3), "ms_per_step": ms, "tokens": T, "hidden": H,
+            "intermediate": inter, "tp": world, "chunks": args.tp_chunks,
+            "gpu_launches_per_step": 5 if world == 1 else 4 + args.tp_chunks,
+            "tensor_frac_per_gpu": per_gpu_ideal_ms / ms, "allreduce_bytes": T * H * 2}
+
+
+def cpu_baseline(target_s: float = 12.0) -> dict:
+    """Oracle GEMM (numpy float32 BLAS, all host threads) on a row sample of 8192^3."""
+    import numpy as np
+
+    from oracle import ops
+
+    M, N, K = HEADLINE
+    rows = 1024
+    rng = np.random.default_rng(0)
+    a = ops.round_to(rng.standard_normal((rows, K), dtype=np.float32), "bfloat16")
+    b = ops.round_to(rng.standard_normal((K, N), dtype=np.float32) * np.float32(K ** -0.5), "bfloat16")
+    ops.gemm(a[:64], b, "bfloat16")  # warm the BLAS thread pool
+    n, t0 = 0, time.perf_counter()
+    while True:
+        ops.gemm(a, b, "bfloat16")
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= target_s or n >= 200:
+            break
+    try:
+        from threadpoolctl import threadpool_info
+
+        cores = max((i.get("num_threads", 1) for i in threadpool_info()), default=os.cpu_count())
+    except Exception:  # noqa: BLE001
+        cores = os.cpu_count()
+    return {"value": 2.0 * rows * N * K * n / el / 1e12, "unit": "TFLOP/s", "cores": cores,
+            "kind": "port",
+            "sample": f"A[{rows} of {M} rows, {K}] x B[{K},{N}] bf16 values, fp32 accumulate, "
+                      f"{n} repetitions in {el:.1f} s (numpy BLAS oracle)"}
+
+
+# ---------------------------------------------------------------- main
+
+def base_line(args, world: int) -> dict:
+    M, N, K = HEADLINE
+    return {
+        "metric": "bf16 GEMM TFLOP/s (M=N=K=8192, fp32 accumulate, bf16 out)",
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: seeded A ~ N(0,1), B ~ N(0,1/K) (Philox on device)",
+        "config": {"workload": "square bf16 GEMM C[8192,8192] = A[8192,8192] B[8192,8192]",
+                   "M": M, "N": N, "K": K,
+                   "parallelism": f"replicas x{world} (one independent GEMM per GPU)",
+                   "l2": "operands 256 MB > 126 MB L2 (no reuse across steps)"},
+    }
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cb = None
+    per_step = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(target_s=1.5)
+        if i >= args.warmup:
+            per_step.append(r)
+        cb = r
+    value = statistics.mean(r["value"] for r in per_step)
+    line = base_line(args, int(os.environ.get("WORLD_SIZE", "1")))
+    line.update({
+        "impl": "reference", "value": value,
+        "ms_per_step": statistics.mean(2.0 * 1024 * 8192 * 8192 / (r["value"] * 1e12) * 1e3
+                                       for r in per_step),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cb["cores"], "kind": "port",
+                         "sample": cb["sample"].split(",")[0] + " per repetition"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    })
+    line["config"]["parallelism"] = "host CPU (oracle port of ref.gemm)"
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    import aot_kernel  # noqa: F401  (fails loudly when the extension is missing)
+    from aot_kernel import capi
+
+    peaks, peak_src = load_peaks()
+    line = base_line(args, world)
+    head = headline_gemm(args, rank, world, peaks)
+    line.update({k: head[k] for k in ("value", "ms_per_step", "roofline", "e2e", "gpu_launches",
+                                      "clocks")})
+    line["roofline"]["peak_source"] = f"{peak_src} (burst bf16 GEMM)"
+    if not args.no_tp:
+        line["tp_mlp"] = tp_mlp(args, rank, world, peaks)
+    if rank == 0 and world == 1 and not args.no_kernels:
+        line["kernels"] = kernel_table(peaks)
+        line["kernels"]["peaks"] = {"hbm_gbs": peaks["hbm_gbs"], "bf16_tflops": peaks["bf16_tflops"],
+                                    "source": peak_src}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline()
+    wd = capi.watchdog_status(local)
+    if wd:
+        line["watchdog"] = wd
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -27,10 +27,15 @@ def _validate(a: torch.Tensor, b: torch.Tensor):
     return device, dtype
 
 
-def gemm(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    """C = A @ B with fp32 accumulation and one rounding to the input dtype."""
+def gemm(a: torch.Tensor, b: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
+    """C = A @ B with fp32 accumulation and one rounding to the input dtype.
+
+    ``out`` (keyword-only, not in the reference signature) may name a
+    contiguous [M, N] tensor to write into, e.g. a row slice of a larger buffer.
+    """
     device, dtype = _validate(a, b)
-    out = torch.empty((a.size(0), b.size(1)), device=device, dtype=dtype)
+    if out is None:
+        out = torch.empty((a.size(0), b.size(1)), device=device, dtype=dtype)
     if dtype in _TENSOR_CORE_DTYPES:
         torch.ops.aot_kernel.gemm_opt(out, a, b)
     else:
