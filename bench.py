@@ -11,8 +11,9 @@ scaling) and ``value`` is the sum over ranks.  The same line carries:
   duration of its launches) against the measured bf16 peak;
 * ``e2e``       - the same metric through the public API with pinned host
   buffers: host->device copy of A and B, the GEMM, device->host copy of C;
-* ``cpu_baseline`` - the oracle's CPU GEMM (numpy, all host threads) on a
-  bounded row sample of the same problem (rank 0, N = 1);
+* ``cpu_baseline`` - the reference's CPU GEMM (``a @ b`` on CPU bf16 tensors,
+  all host threads) on a bounded row sample of the same problem, with the
+  numpy oracle's rate beside it (rank 0, N = 1);
 * ``kernels``   - the remaining workloads of the path at their configured sizes:
   the square sweep, the Llama-3-8B linear layers from decode to prefill,
   rms_norm, silu and silu(gate)*up, each with its roofline fraction (N = 1);
@@ -20,9 +21,12 @@ scaling) and ``value`` is the sum over ranks.  The same line carries:
   hidden 8192, intermediate 28672) tensor-parallel over the N ranks with one
   NCCL all-reduce (the multi-GPU path; strong scaling in tokens).
 
-``--impl reference`` times the reference's CPU path (the oracle port of
-``ref.gemm``, all host threads) on the same metric instead; under torchrun
+``--impl reference`` times the reference's CPU path (``ref.gemm`` = ``a @ b``
+on CPU tensors, all host threads) on the same metric instead; under torchrun
 only rank 0 runs it.
+
+``--case NAME`` runs only NAME's launches (warmup + steps) and prints nothing
+else: the command the committed ncu summaries under profiles/ were made with.
 """
 
 from __future__ import annotations
@@ -50,6 +54,19 @@ HEADLINE = (8192, 8192, 8192)
 L2_BYTES = 126 * 1024 * 1024
 
 
+# --case workloads: name -> (kind, shape)
+CASES = {
+    "gemm_8192": ("gemm", (8192, 8192, 8192)),
+    "gemm_4096": ("gemm", (4096, 4096, 4096)),
+    "gemm_decode_m1": ("gemm", (1, 4096, 28672)),
+    "gemm_decode_m16": ("gemm", (16, 4096, 28672)),
+    "gemm_m128_down": ("gemm", (128, 14336, 4096)),
+    "rms_norm": ("rms_norm", (8192, 4096)),
+    "silu": ("silu", (8192, 14336)),
+    "silu_mul": ("silu_mul", (8192, 14336)),
+}
+
+
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
@@ -60,6 +77,8 @@ def parse_args():
     ap.add_argument("--no-tp", action="store_true", help="skip the tensor-parallel MLP block")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--tp-chunks", type=int, default=1)
+    ap.add_argument("--case", choices=sorted(CASES), default=None,
+                    help="run only this workload's launches (for profilers)")
     return ap.parse_args()
 
 
@@ -368,35 +387,46 @@ def tp_mlp(args, rank: int, world: int, peaks: dict) -> dict:
             "tensor_frac_per_gpu": per_gpu_ideal_ms / ms, "allreduce_bytes": T * H * 2}
 
 
-def cpu_baseline(target_s: float = 12.0) -> dict:
-    """Oracle GEMM (numpy float32 BLAS, all host threads) on a row sample of 8192^3."""
+def cpu_baseline(target_s: float = 8.0) -> dict:
+    """The reference's CPU GEMM on a bounded row sample of the 8192^3 problem.
+
+    ``ref.gemm`` is ``a @ b`` (ref/gemm.py:4-5); on CPU bf16 tensors torch runs
+    it through its own bf16 GEMM with every host thread.  That call, ported
+    as one line, is the timed value.  The numpy oracle (float32 BLAS) is timed
+    beside it for reference.
+    """
     import numpy as np
+    import torch
 
     from oracle import ops
 
     M, N, K = HEADLINE
     rows = 1024
-    rng = np.random.default_rng(0)
-    a = ops.round_to(rng.standard_normal((rows, K), dtype=np.float32), "bfloat16")
-    b = ops.round_to(rng.standard_normal((K, N), dtype=np.float32) * np.float32(K ** -0.5), "bfloat16")
-    ops.gemm(a[:64], b, "bfloat16")  # warm the BLAS thread pool
-    n, t0 = 0, time.perf_counter()
-    while True:
-        ops.gemm(a, b, "bfloat16")
-        n += 1
-        el = time.perf_counter() - t0
-        if el >= target_s or n >= 200:
-            break
-    try:
-        from threadpoolctl import threadpool_info
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(0)
+    a = torch.randn((rows, K), generator=g).to(torch.bfloat16)
+    b = (torch.randn((K, N), generator=g) * K ** -0.5).to(torch.bfloat16)
 
-        cores = max((i.get("num_threads", 1) for i in threadpool_info()), default=os.cpu_count())
-    except Exception:  # noqa: BLE001
-        cores = os.cpu_count()
-    return {"value": 2.0 * rows * N * K * n / el / 1e12, "unit": "TFLOP/s", "cores": cores,
+    def timed(fn, budget):
+        fn()  # warm thread pools / packing
+        n, t0 = 0, time.perf_counter()
+        while True:
+            fn()
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= budget or n >= 500:
+                return n, el
+
+    n, el = timed(lambda: a @ b, target_s)
+    a_np, b_np = a.float().numpy(), b.float().numpy()
+    n_np, el_np = timed(lambda: ops.gemm(a_np, b_np, "bfloat16"), target_s / 2)
+    flops = 2.0 * rows * N * K
+    return {"value": flops * n / el / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
             "kind": "port",
-            "sample": f"A[{rows} of {M} rows, {K}] x B[{K},{N}] bf16 values, fp32 accumulate, "
-                      f"{n} repetitions in {el:.1f} s (numpy BLAS oracle)"}
+            "sample": f"A[{rows} of {M} rows, {K}] @ B[{K},{N}] bf16 on CPU via torch (the call "
+                      f"ref.gemm makes), {n} repetitions in {el:.1f} s",
+            "oracle_numpy_tflops": flops * n_np / el_np / 1e12,
+            "cpu_count": os.cpu_count()}
 
 
 # ---------------------------------------------------------------- main
@@ -428,7 +458,7 @@ def run_reference(args) -> None:
     cb = None
     per_step = []
     for i in range(args.warmup + args.steps):
-        r = cpu_baseline(target_s=1.5)
+        r = cpu_baseline(target_s=1.0)
         if i >= args.warmup:
             per_step.append(r)
         cb = r
@@ -439,18 +469,48 @@ def run_reference(args) -> None:
         "ms_per_step": statistics.mean(2.0 * 1024 * 8192 * 8192 / (r["value"] * 1e12) * 1e3
                                        for r in per_step),
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cb["cores"], "kind": "port",
-                         "sample": cb["sample"].split(",")[0] + " per repetition"},
+                         "sample": cb["sample"]},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
     })
-    line["config"]["parallelism"] = "host CPU (oracle port of ref.gemm)"
+    line["config"]["parallelism"] = "host CPU, all threads (ref.gemm = a @ b on CPU tensors)"
     print(json.dumps(line), flush=True)
+
+
+def run_case(args) -> None:
+    import torch
+
+    import aot_kernel
+
+    kind, shape = CASES[args.case]
+    if kind == "gemm":
+        M, K, N = shape
+        a = rand_bf16((M, K), 1)
+        b = rand_bf16((K, N), 2, std=0.02)
+        fn = lambda: aot_kernel.gemm(a, b)  # noqa: E731
+    elif kind == "rms_norm":
+        x = rand_bf16(shape, 3)
+        w = rand_bf16((shape[1],), 4, std=0.1, mean=1.0)
+        fn = lambda: aot_kernel.rms_norm(x, w)  # noqa: E731
+    elif kind == "silu":
+        x = rand_bf16(shape, 5, std=2.0)
+        fn = lambda: aot_kernel.silu(x)  # noqa: E731
+    else:
+        g = rand_bf16(shape, 6, std=2.0)
+        u = rand_bf16(shape, 7, std=2.0)
+        fn = lambda: aot_kernel.silu_mul(g, u)  # noqa: E731
+    for _ in range(args.warmup + args.steps):
+        fn()
+    torch.cuda.synchronize()
 
 
 def main() -> None:
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.case:
+        run_case(args)
         return
     import torch
     import torch.distributed as dist
