@@ -32,14 +32,10 @@ else: the command the committed ncu summaries under profiles/ were made with.
 from __future__ import annotations
 
 import argparse
-import csv
-import io
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 from datetime import timedelta
 from pathlib import Path
@@ -96,59 +92,82 @@ def load_peaks() -> tuple[dict, str]:
 # ---------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples every 200 ms while active."""
+    """Samples this rank's GPU clock, power and clock-event reasons through NVML
+    (read-only queries) every 10 ms while the timed region runs."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
+               "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
+               "sw_thermal_slowdown": "nvmlClocksEventReasonSwThermalSlowdown",
+               "sw_power_cap": "nvmlClocksEventReasonSwPowerCap",
+               "hw_power_brake": "nvmlClocksEventReasonHwPowerBrakeSlowdown"}
 
-    def __init__(self):
-        self.proc = None
-        self.file = None
+    def __init__(self, device: int = 0, period_s: float = 0.01):
+        self.device, self.period = device, period_s
+        self.samples: list[tuple[float, float, int]] = []
+        self.max_mhz = None
+        self._stop = None
+        self._thread = None
+        self._nvml = None
+
+    def _handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        try:
+            bus = torch.cuda.get_device_properties(self.device).pci_bus_id
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:  # noqa: BLE001
+            return pynvml.nvmlDeviceGetHandleByIndex(self.device)
+
+    def _run(self, h):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((float(sm), pw, int(rs)))
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(self.period)
 
     def __enter__(self):
-        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        import threading
+
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
-        except OSError:
-            self.proc = None
+            import pynvml
+
+            self._nvml = pynvml
+            h = self._handle()
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        except Exception:  # noqa: BLE001
+            self._nvml = None
+            return self
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, args=(h,), daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
         return False
 
-    def summary(self, devices: set[int] | None = None) -> dict:
-        self.file.flush()
-        self.file.seek(0)
-        rows = list(csv.reader(io.StringIO(self.file.read())))
-        os.unlink(self.file.name)
-        mhz, max_mhz, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            if len(r) < 9:
-                continue
-            try:
-                idx, sm, smax, power = int(r[0]), float(r[1]), float(r[2]), float(r[3])
-            except ValueError:
-                continue
-            if devices is not None and idx not in devices:
-                continue
-            max_mhz = max(max_mhz, smax)
-            if power > 300.0 or sm > 1000.0:  # under load
-                mhz.append(sm)
-            for name, v in zip(names, r[5:9]):
-                if v.strip().lower() == "active":
+    def summary(self) -> dict:
+        if self._nvml is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        loaded = [s for s in self.samples if s[1] > 250.0] or self.samples
+        reasons = set()
+        for _, _, bits in loaded:
+            for name, const in self.REASONS.items():
+                if bits & int(getattr(self._nvml, const, 0)):
                     reasons.add(name)
-        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": max_mhz or None,
-                "reasons": sorted(reasons), "samples_under_load": len(mhz)}
+        return {"sm_mhz": statistics.median(s[0] for s in loaded) if loaded else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons),
+                "samples": len(self.samples), "samples_under_load": len(loaded),
+                "power_w_max": max((s[1] for s in self.samples), default=None)}
 
 
 # ---------------------------------------------------------------- timing helpers
@@ -219,7 +238,7 @@ def headline_gemm(args, rank: int, world: int, peaks: dict):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    with ClockSampler() as clocks:
+    with ClockSampler(torch.cuda.current_device()) as clocks:
         events = []
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
