@@ -193,12 +193,18 @@ def per_launch_ms(fn, iters: int, warmup: int, flush=None) -> list[float]:
 
 
 def make_flush():
+    """Evicts the timed kernel's data from L2 by reading 2x L2 of other data.
+
+    A read sweep leaves clean lines behind; a write sweep would leave up to
+    126 MB of dirty lines whose write-back the next timed launch would pay.
+    """
     import torch
 
-    buf = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
+    buf = torch.ones(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
+    sink = torch.empty((), dtype=torch.float32, device="cuda")
 
     def flush():
-        buf.fill_(1.0)
+        torch.sum(buf, out=sink)
 
     return flush
 
