@@ -114,10 +114,12 @@ class ClockSampler:
         import torch
 
         pynvml.nvmlInit()
+        p = torch.cuda.get_device_properties(self.device)
+        # torch reports the PCI location as integers; NVML wants "DDDDDDDD:BB:DD.0".
+        bus_id = f"{int(p.pci_domain_id):08X}:{int(p.pci_bus_id):02X}:{int(p.pci_device_id):02X}.0"
         try:
-            bus = torch.cuda.get_device_properties(self.device).pci_bus_id
-            return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
-        except Exception:  # noqa: BLE001
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus_id.encode())
+        except pynvml.NVMLError:
             return pynvml.nvmlDeviceGetHandleByIndex(self.device)
 
     def _run(self, h):

@@ -249,8 +249,15 @@ int launch_skinny(void* c, const void* a, const void* b, int M, int N, int K, bo
 
   const int ntiles = (N + kTileN - 1) / kTileN;
   const int kblocks = (K + kBK - 1) / kBK;
-  const int target = 2 * info.sm_count;  // two resident CTAs per SM
-  int S = (target + ntiles - 1) / ntiles;
+  // One wave: every CTA streams an equal share of the weight at the same time,
+  // so the split is the number of resident CTAs per column strip (rounded
+  // down; rounding up would leave a partial second wave).
+  int per_sm = 0;
+  cudaError_t oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads,
+                                                                 L::kAlloc);
+  if (oe != cudaSuccess || per_sm < 1) per_sm = 1;
+  const int capacity = per_sm * info.sm_count;
+  int S = capacity / ntiles;
   if (S > kMaxCluster) S = kMaxCluster;
   if (S > kblocks) S = kblocks;
   if (S < 1) S = 1;

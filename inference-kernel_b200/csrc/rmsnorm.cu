@@ -18,6 +18,24 @@ namespace {
 constexpr int kBlock = 256;
 
 template <typename T, int VPT, int TPR>
+__device__ __forceinline__ void load_row(const T* __restrict__ x, int64_t row, int64_t rows,
+                                         int cols, int t, uint4 (&v)[VPT]) {
+  constexpr int E = Elem<T>::kPerVec;
+  const int n_vec = cols / E;
+  const bool live = row < rows;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (live ? row : 0) * (int64_t)cols);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = t + i * TPR;
+    if (live && idx < n_vec) v[i] = ld_stream(xr + idx);
+    else v[i] = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+// Persistent over row groups: a block owns RPB rows at a time and, before
+// reducing them, issues the loads of the group it will handle next, so each
+// SM keeps two groups of rows in flight and the grid is a single wave.
+template <typename T, int VPT, int TPR>
 __global__ void __launch_bounds__(TPR > kBlock ? TPR : kBlock)
     rmsnorm_vec_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y,
                        int64_t rows, int cols, float eps) {
@@ -25,55 +43,63 @@ __global__ void __launch_bounds__(TPR > kBlock ? TPR : kBlock)
   constexpr int THREADS = TPR > kBlock ? TPR : kBlock;
   constexpr int RPB = THREADS / TPR;  // rows per block
   constexpr int WPR = TPR / 32;       // warps per row
-  __shared__ float partial[RPB][WPR > 1 ? WPR : 1];
+  // 1024-thread blocks get 64 registers per thread: no room for a second row copy.
+  constexpr bool kPrefetch = THREADS < 1024;
+  __shared__ float partial[2][RPB][WPR > 1 ? WPR : 1];
 
   const int sub = threadIdx.x / TPR;  // row slot in this block
   const int t = threadIdx.x % TPR;    // thread index within the row
-  const int64_t row = (int64_t)blockIdx.x * RPB + sub;
-  const bool live = row < rows;
   const int n_vec = cols / E;
-
-  const uint4* xr = reinterpret_cast<const uint4*>(x + (live ? row : 0) * (int64_t)cols);
-  uint4 v[VPT];
-#pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int idx = t + i * TPR;
-    if (live && idx < n_vec) v[i] = ld_stream(xr + idx);
-    else v[i] = make_uint4(0u, 0u, 0u, 0u);
-  }
-  float ss = 0.0f;
-#pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    float f[E];
-    Elem<T>::unpack(v[i], f);
-#pragma unroll
-    for (int e = 0; e < E; ++e) ss = fmaf(f[e], f[e], ss);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if constexpr (WPR > 1) {
-    const int warp_in_row = t / 32;
-    if ((t & 31) == 0) partial[sub][warp_in_row] = ss;
-    __syncthreads();
-    ss = 0.0f;
-#pragma unroll
-    for (int k = 0; k < WPR; ++k) ss += partial[sub][k];
-  }
-  const float rstd = rsqrtf(ss / (float)cols + eps);
-  if (!live) return;
-
+  const int64_t groups = (rows + RPB - 1) / RPB;
   const uint4* wr = reinterpret_cast<const uint4*>(w);
-  uint4* yr = reinterpret_cast<uint4*>(y + row * (int64_t)cols);
+
+  uint4 cur[VPT];
+  int64_t g = blockIdx.x;
+  load_row<T, VPT, TPR>(x, g * RPB + sub, rows, cols, t, cur);
+  for (int iter = 0; g < groups; g += gridDim.x, ++iter) {
+    uint4 nxt[VPT];
+    if constexpr (kPrefetch) load_row<T, VPT, TPR>(x, (g + gridDim.x) * RPB + sub, rows, cols, t, nxt);
+
+    float ss = 0.0f;
 #pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int idx = t + i * TPR;
-    if (idx < n_vec) {
-      float f[E], g[E];
-      Elem<T>::unpack(v[i], f);
-      Elem<T>::unpack(ld_cached(wr + idx), g);
+    for (int i = 0; i < VPT; ++i) {
+      float f[E];
+      Elem<T>::unpack(cur[i], f);
 #pragma unroll
-      for (int e = 0; e < E; ++e) f[e] = f[e] * rstd * g[e];
-      st_stream(yr + idx, Elem<T>::pack(f));
+      for (int e = 0; e < E; ++e) ss = fmaf(f[e], f[e], ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if constexpr (WPR > 1) {
+      // Two partial buffers alternate so one barrier per group suffices.
+      if ((t & 31) == 0) partial[iter & 1][sub][t / 32] = ss;
+      __syncthreads();
+      ss = 0.0f;
+#pragma unroll
+      for (int k = 0; k < WPR; ++k) ss += partial[iter & 1][sub][k];
+    }
+    const float rstd = rsqrtf(ss / (float)cols + eps);
+    const int64_t row = g * RPB + sub;
+    if (row < rows) {
+      uint4* yr = reinterpret_cast<uint4*>(y + row * (int64_t)cols);
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int idx = t + i * TPR;
+        if (idx < n_vec) {
+          float f[E], gw[E];
+          Elem<T>::unpack(cur[i], f);
+          Elem<T>::unpack(ld_cached(wr + idx), gw);
+#pragma unroll
+          for (int e = 0; e < E; ++e) f[e] = f[e] * rstd * gw[e];
+          st_stream(yr + idx, Elem<T>::pack(f));
+        }
+      }
+    }
+    if constexpr (kPrefetch) {
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) cur[i] = nxt[i];
+    } else {
+      load_row<T, VPT, TPR>(x, (g + gridDim.x) * RPB + sub, rows, cols, t, cur);
     }
   }
 }
@@ -109,8 +135,17 @@ template <typename T, int VPT, int TPR>
 int launch_vec(const T* x, const T* w, T* y, int64_t rows, int cols, float eps, cudaStream_t s) {
   constexpr int THREADS = TPR > kBlock ? TPR : kBlock;
   constexpr int RPB = THREADS / TPR;
-  const int64_t blocks = (rows + RPB - 1) / RPB;
-  rmsnorm_vec_kernel<T, VPT, TPR><<<(unsigned)blocks, THREADS, 0, s>>>(x, w, y, rows, cols, eps);
+  DeviceInfo info;
+  if (int st = current_device_info(&info)) return st;
+  auto kernel = rmsnorm_vec_kernel<T, VPT, TPR>;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, THREADS, 0) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  const int64_t groups = (rows + RPB - 1) / RPB;
+  const int64_t capacity = (int64_t)per_sm * info.sm_count;
+  const int64_t blocks = groups < capacity ? groups : capacity;
+  kernel<<<(unsigned)blocks, THREADS, 0, s>>>(x, w, y, rows, cols, eps);
   return check_launch("aotk_rmsnorm_forward");
 }
 
