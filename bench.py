@@ -206,7 +206,7 @@ def make_flush():
     sink = torch.empty((), dtype=torch.float32, device="cuda")
 
     def flush():
-        torch.sum(buf, out=sink)
+        torch.sum(buf, dim=0, out=sink)
 
     return flush
 
