@@ -172,45 +172,6 @@ class ClockSampler:
                 "power_w_max": max((s[1] for s in self.samples), default=None)}
 
 
-# ---------------------------------------------------------------- timing helpers
-
-def per_launch_ms(fn, iters: int, warmup: int, flush=None) -> list[float]:
-    """CUDA-event duration of each of `iters` launches of fn() on the current stream."""
-    import torch
-
-    for _ in range(warmup):
-        fn()
-    torch.cuda.synchronize()
-    times = []
-    for _ in range(iters):
-        if flush is not None:
-            flush()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        fn()
-        e.record()
-        times.append((s, e))
-    torch.cuda.synchronize()
-    return [s.elapsed_time(e) for s, e in times]
-
-
-def make_flush():
-    """Evicts the timed kernel's data from L2 by reading 2x L2 of other data.
-
-    A read sweep leaves clean lines behind; a write sweep would leave up to
-    126 MB of dirty lines whose write-back the next timed launch would pay.
-    """
-    import torch
-
-    buf = torch.ones(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
-    sink = torch.empty((), dtype=torch.float32, device="cuda")
-
-    def flush():
-        torch.sum(buf, dim=0, out=sink)
-
-    return flush
-
-
 # ---------------------------------------------------------------- workloads
 
 def rand_bf16(shape, seed: int, std: float = 1.0, mean: float = 0.0):
@@ -324,20 +285,59 @@ def traffic_per_launch(key: str):
         return None
 
 
+def graph_launch_ms(calls, replays: int = 4) -> float:
+    """Mean device time of one launch: the launches in `calls` (one per input
+    set, the sets together larger than L2) are captured once into a CUDA graph
+    and the graph is replayed back to back; host dispatch is not timed."""
+    import torch
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for c in calls:  # first calls set per-device kernel attributes
+            c()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for c in calls:
+            c()
+    g.replay()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(replays):
+        g.replay()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / (replays * len(calls))
+    del g
+    return ms
+
+
+def _sets_for(nbytes: int, cap: int = 16) -> int:
+    """Input copies needed for a rotation of at least 2x L2."""
+    return max(1, min(cap, -(-2 * L2_BYTES // max(1, nbytes))))
+
+
 def kernel_table(peaks: dict) -> dict:
-    """Every configured workload of the path, timed per launch with an L2 flush in between."""
+    """Every configured workload of the path, timed from CUDA-graph replays."""
     import torch
 
     import aot_kernel
 
-    flush = make_flush()
     out = {}
     ridge = peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
 
     def gemm_entry(M, K, N, seed, b_std):
-        a = rand_bf16((M, K), seed)
-        b = rand_bf16((K, N), seed + 1, std=b_std)
-        ms = statistics.mean(per_launch_ms(lambda: aot_kernel.gemm(a, b), 10, 3, flush))
+        nbytes = 2 * (M * K + K * N)
+        R = _sets_for(nbytes)
+        sets = [(rand_bf16((M, K), seed + 2 * i), rand_bf16((K, N), seed + 2 * i + 1, std=b_std))
+                for i in range(R)]
+        outs = [torch.empty((M, N), device="cuda", dtype=torch.bfloat16) for _ in range(R)]
+        calls = [lambda a=a, b=b, c=c: aot_kernel.gemm(a, b, out=c) for (a, b), c in zip(sets, outs)]
+        ms = graph_launch_ms(calls)
+        del sets, outs, calls
         flops = 2.0 * M * N * K
         nbytes = 2.0 * (M * K + K * N + M * N)
         tf = flops / (ms * 1e-3) / 1e12
@@ -345,28 +345,36 @@ def kernel_table(peaks: dict) -> dict:
         bound = "tensor" if flops / nbytes >= ridge else "hbm"
         frac = tf / peaks["bf16_tflops"] if bound == "tensor" else gbs / peaks["hbm_gbs"]
         return {"ms": round(ms, 5), "tflops": round(tf, 2), "gbs": round(gbs, 1), "bound": bound,
-                "frac": round(frac, 4)}
+                "frac": round(frac, 4), "input_sets": R}
 
     for n in (2048, 4096, 8192, 16384):
         out[f"gemm_{n}^3"] = gemm_entry(n, n, n, 10 + n, n ** -0.5)
     for K, N in ((4096, 6144), (4096, 28672), (14336, 4096)):
         for M in (1, 16, 128, 2048, 8192):
             out[f"linear_M{M}_K{K}_N{N}"] = gemm_entry(M, K, N, M + K + N, 0.02)
+    torch.cuda.empty_cache()
 
-    def hbm_entry(fn, nbytes):
-        ms = statistics.mean(per_launch_ms(fn, 20, 3, flush))
+    def hbm_entry(calls, nbytes, R):
+        ms = graph_launch_ms(calls)
         gbs = nbytes / (ms * 1e-3) / 1e9
         return {"ms": round(ms, 5), "gbs": round(gbs, 1), "bound": "hbm",
-                "frac": round(gbs / peaks["hbm_gbs"], 4), "bytes": int(nbytes)}
+                "frac": round(gbs / peaks["hbm_gbs"], 4), "bytes": int(nbytes), "input_sets": R}
 
-    x = rand_bf16((8192, 4096), 20)
-    w = rand_bf16((4096,), 21, std=0.1, mean=1.0)
-    out["rms_norm_8192x4096"] = hbm_entry(lambda: aot_kernel.rms_norm(x, w), 2 * x.nbytes + w.nbytes)
-    del x
-    g = rand_bf16((8192, 14336), 22, std=2.0)
-    u = rand_bf16((8192, 14336), 23, std=2.0)
-    out["silu_8192x14336"] = hbm_entry(lambda: aot_kernel.silu(g), 2 * g.nbytes)
-    out["silu_mul_8192x14336"] = hbm_entry(lambda: aot_kernel.silu_mul(g, u), 3 * g.nbytes)
+    rows, cols = 8192, 4096
+    R = _sets_for(rows * cols * 2)
+    w = rand_bf16((cols,), 21, std=0.1, mean=1.0)
+    xs = [rand_bf16((rows, cols), 20 + 2 * i) for i in range(R)]
+    out["rms_norm_8192x4096"] = hbm_entry([lambda x=x: aot_kernel.rms_norm(x, w) for x in xs],
+                                          2.0 * rows * cols * 2 + cols * 2, R)
+    del xs
+    rows, cols = 8192, 14336
+    g = rand_bf16((rows, cols), 22, std=2.0)
+    u = rand_bf16((rows, cols), 23, std=2.0)
+    out["silu_8192x14336"] = hbm_entry([lambda: aot_kernel.silu(g), lambda: aot_kernel.silu(u)],
+                                       2.0 * rows * cols * 2, 2)
+    out["silu_mul_8192x14336"] = hbm_entry([lambda: aot_kernel.silu_mul(g, u),
+                                            lambda: aot_kernel.silu_mul(u, g)],
+                                           3.0 * rows * cols * 2, 2)
     del g, u
     torch.cuda.empty_cache()
     return out
