@@ -414,12 +414,49 @@ def tp_mlp(args, rank: int, world: int, peaks: dict) -> dict:
     if world > 1:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms = float(ms.item())
+    phases = tp_phase_breakdown(block, x, world)
     flops = 2.0 * T * H * 2 * inter + 2.0 * T * inter * H
     per_gpu_ideal_ms = flops / world / (peaks["bf16_tflops"] * 1e12) * 1e3
     return {"tokens_per_s": T / (ms * 1e-3), "ms_per_step": ms, "tokens": T, "hidden": H,
             "intermediate": inter, "tp": world, "chunks": args.tp_chunks,
             "gpu_launches_per_step": 5 if world == 1 else 4 + args.tp_chunks,
-            "tensor_frac_per_gpu": per_gpu_ideal_ms / ms, "allreduce_bytes": T * H * 2}
+            "tensor_frac_per_gpu": per_gpu_ideal_ms / ms, "allreduce_bytes": T * H * 2,
+            "phases_ms": phases}
+
+
+def tp_phase_breakdown(block, x, world: int, reps: int = 5) -> dict:
+    """Device time of each op of one block step (mean of `reps` untimed-region
+    passes, CUDA events between ops, max over ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    ops, s = block.ops, block.shard
+    names = ["rms_norm", "gemm_gate_up", "silu_mul", "gemm_down", "all_reduce"]
+    acc = torch.zeros(len(names), dtype=torch.float64, device="cuda")
+    for _ in range(reps):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ev[0].record()
+        h = ops.rms_norm(x, s.norm_weight, block.eps)
+        ev[1].record()
+        gu = ops.gemm(h, s.w_gate_up)
+        ev[2].record()
+        act = ops.silu_mul(gu[:, :block.inter_local], gu[:, block.inter_local:])
+        ev[3].record()
+        out = ops.gemm(act, s.w_down)
+        ev[4].record()
+        if world > 1:
+            dist.all_reduce(out)
+        ev[5].record()
+        torch.cuda.synchronize()
+        acc += torch.tensor([ev[i].elapsed_time(ev[i + 1]) for i in range(len(names))],
+                            dtype=torch.float64, device="cuda")
+    acc /= reps
+    if world > 1:
+        dist.all_reduce(acc, op=dist.ReduceOp.MAX)
+    return {n: round(v, 4) for n, v in zip(names, acc.tolist())}
 
 
 def cpu_baseline(target_s: float = 8.0) -> dict:

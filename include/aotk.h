@@ -23,6 +23,7 @@
 #ifndef AOTK_H_
 #define AOTK_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #if defined(__GNUC__)
@@ -98,6 +99,21 @@ AOTK_API int aotk_rmsnorm_forward(void* out, const void* x, const void* weight, 
  * (aot_kernel/csrc/gemm/gemm_opt.cu:165-195, registration.cc:23-24). */
 AOTK_API int aotk_gemm_opt(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
                   int dtype, void* stream);
+
+/* aotk_gemm_opt with caller-provided scratch.  Bytes needed for (M, N, K,
+ * dtype) on the current device come from aotk_gemm_opt_workspace_size (0 when
+ * the problem has no use for it).  With at least that many bytes, 256-byte
+ * aligned (contents irrelevant: the call resets what it uses), the persistent
+ * kernel splits the tiles of its partial last wave along K across all SMs and
+ * reduces the fp32 partials in split order, so results stay deterministic.
+ * With less, it behaves exactly like aotk_gemm_opt.  Calls that share a
+ * workspace must be ordered on one stream.
+ * Same reference counterpart as aotk_gemm_opt. */
+AOTK_API int aotk_gemm_opt_ws(void* c, const void* a, const void* b, int64_t M, int64_t N,
+                              int64_t K, int dtype, void* workspace, size_t workspace_bytes,
+                              void* stream);
+AOTK_API int aotk_gemm_opt_workspace_size(int64_t M, int64_t N, int64_t K, int dtype,
+                                          size_t* bytes);
 
 /* Any-dtype, any-shape GEMM (SIMT, fp32 accumulation).
  * Replaces gemm(Tensor! out, Tensor a, Tensor b)

@@ -30,6 +30,8 @@ SIGNATURES: dict[str, list] = {
     "aotk_silu_mul_forward": [_ptr, _i64, _ptr, _i64, _ptr, _i64, _i64, _i64, _int, _ptr],
     "aotk_rmsnorm_forward": [_ptr, _ptr, _ptr, _i64, _i64, ctypes.c_double, _int, _ptr],
     "aotk_gemm_opt": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
+    "aotk_gemm_opt_ws": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr, ctypes.c_size_t, _ptr],
+    "aotk_gemm_opt_workspace_size": [_i64, _i64, _i64, _int, ctypes.POINTER(ctypes.c_size_t)],
     "aotk_gemm": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
     "aotk_gemm_tc": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
     "aotk_gemm_skinny": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
@@ -123,6 +125,17 @@ def _gemm(name, c, a, b, M, N, K, dtype, stream) -> None:
 
 def gemm_opt(c, a, b, M, N, K, dtype, stream=None) -> None:
     _gemm("aotk_gemm_opt", c, a, b, M, N, K, dtype, stream)
+
+
+def gemm_opt_workspace_size(M, N, K, dtype) -> int:
+    n = ctypes.c_size_t(0)
+    _call("aotk_gemm_opt_workspace_size", M, N, K, dtype, ctypes.byref(n))
+    return n.value
+
+
+def gemm_opt_ws(c, a, b, M, N, K, dtype, workspace, workspace_bytes, stream=None) -> None:
+    _call("aotk_gemm_opt_ws", _p(c), _p(a), _p(b), M, N, K, dtype, _p(workspace), workspace_bytes,
+          _stream(stream))
 
 
 def gemm(c, a, b, M, N, K, dtype, stream=None) -> None:

@@ -1,6 +1,7 @@
 // C-ABI GEMM entry points and the path selection of aotk_gemm_opt.
 //
-// Path choice (all fp32 accumulation, one rounding per output):
+// Path choice (all fp32 accumulation, one rounding per output; with a
+// workspace the persistent kernel also splits its partial last wave along K):
 //   16-bit, TMA-addressable, M <= 128  -> skinny swap-AB split-K kernel
 //                                          (decode; HBM-bound on the weight)
 //   16-bit, TMA-addressable, M > 128   -> persistent tcgen05 kernel
@@ -88,8 +89,9 @@ int check_tc_preconditions(const char* who, const void* c, const void* a, const 
 
 }  // namespace aotk
 
-extern "C" int aotk_gemm_opt(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
-                             int dtype, void* stream) {
+extern "C" int aotk_gemm_opt_ws(void* c, const void* a, const void* b, int64_t M, int64_t N,
+                                int64_t K, int dtype, void* workspace, size_t workspace_bytes,
+                                void* stream) {
   using namespace aotk;
   if (int st = validate_common("aotk_gemm_opt", c, a, b, M, N, K, dtype)) return st;
   if (dtype == AOTK_FLOAT32)
@@ -98,9 +100,29 @@ extern "C" int aotk_gemm_opt(void* c, const void* a, const void* b, int64_t M, i
   if (K == 0) return zero_output(c, M, N, dtype, stream);
   if (tc_eligible(c, a, b, M, N, K, dtype)) {
     if (M <= kSkinnyMaxM) return gemm_skinny(c, a, b, M, N, K, dtype, stream);
-    return gemm_tc(c, a, b, M, N, K, dtype, stream);
+    return gemm_tc(c, a, b, M, N, K, dtype, workspace, workspace_bytes, stream);
   }
   return gemm_simt(c, a, b, M, N, K, dtype, stream);
+}
+
+extern "C" int aotk_gemm_opt(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
+                             int dtype, void* stream) {
+  return aotk_gemm_opt_ws(c, a, b, M, N, K, dtype, nullptr, 0, stream);
+}
+
+extern "C" int aotk_gemm_opt_workspace_size(int64_t M, int64_t N, int64_t K, int dtype,
+                                            size_t* bytes) {
+  using namespace aotk;
+  if (!bytes) return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_gemm_opt_workspace_size: null pointer");
+  *bytes = 0;
+  if (M < 0 || N < 0 || K < 0)
+    return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_gemm_opt_workspace_size: negative size");
+  if (dtype != AOTK_FLOAT16 && dtype != AOTK_BFLOAT16) return AOTK_OK;
+  if (M <= kSkinnyMaxM || K % 8 != 0 || N % 8 != 0) return AOTK_OK;
+  DeviceInfo info;
+  if (int st = current_device_info(&info)) return st;
+  *bytes = gemm_tc_workspace_size(M, N, K, info.sm_count);
+  return AOTK_OK;
 }
 
 extern "C" int aotk_gemm(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
@@ -113,7 +135,7 @@ extern "C" int aotk_gemm(void* c, const void* a, const void* b, int64_t M, int64
 
 extern "C" int aotk_gemm_tc(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
                             int dtype, void* stream) {
-  return aotk::gemm_tc(c, a, b, M, N, K, dtype, stream);
+  return aotk::gemm_tc(c, a, b, M, N, K, dtype, nullptr, 0, stream);
 }
 
 extern "C" int aotk_gemm_skinny(void* c, const void* a, const void* b, int64_t M, int64_t N,

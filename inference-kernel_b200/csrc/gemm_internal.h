@@ -7,9 +7,12 @@
 
 namespace aotk {
 
-// Persistent tcgen05 kernel (gemm_tc.cu).
+// Persistent tcgen05 kernel (gemm_tc.cu).  With a workspace of at least
+// gemm_tc_workspace_size() bytes (256-byte aligned, contents irrelevant) the
+// partial last wave of tiles is split along K; without one it runs whole.
 int gemm_tc(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K, int dtype,
-            void* stream);
+            void* workspace, size_t ws_bytes, void* stream);
+size_t gemm_tc_workspace_size(int64_t M, int64_t N, int64_t K, int sm_count);
 
 // Swap-AB split-K tcgen05 kernel for M <= kSkinnyMaxM (gemm_skinny.cu).
 constexpr int64_t kSkinnyMaxM = 128;

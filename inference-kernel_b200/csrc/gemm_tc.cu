@@ -16,6 +16,12 @@
 //               buffered per warp).  The accumulator is handed back as soon
 //               as it is read, so the next tile's main loop overlaps this
 //               tile's stores.
+// Schedule: whole tiles are dealt round-robin to the CTAs; when the tile count
+// leaves a partial last wave, those last tiles are instead cut along K into S
+// units spread over all SMs.  A unit writes its fp32 partial tile to a
+// caller-provided workspace; the unit that finishes last (atomic counter per
+// tile) sums the S partials in split order and stores the 16-bit result, so
+// the output is deterministic.  Without a workspace the last wave runs whole.
 // Every pipeline wait is bounded (sm100.cuh): on a timeout the kernel records
 // a watchdog bit, lets the other roles drop out, drains its in-flight copies
 // and frees TMEM before returning.
@@ -74,10 +80,55 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
   nb = local / gm;
 }
 
+// Work list shared by the producer, MMA and epilogue roles of a CTA.
+struct TcSched {
+  int tiles_m, tiles_n, num_tiles, kblocks;
+  int full_rounds;    // rounds of whole tiles: tile = cta + r * grid, tile < split_begin
+  int split_begin;    // first tile computed in K splits (num_tiles when none)
+  int splits;         // units per split tile
+  int kb_per_split;
+  int units;          // (num_tiles - split_begin) * splits
+  float* ws;          // [units][kBM][BN] fp32 partial tiles
+  unsigned* counters; // [num_tiles - split_begin] arrivals per split tile
+};
+
+struct WorkItem {
+  int tile, kb0, kb1, unit;  // unit < 0: whole tile
+};
+
+__device__ __forceinline__ bool work_item(const TcSched& s, int i, WorkItem& w) {
+  if (i < s.full_rounds) {
+    w.tile = blockIdx.x + i * gridDim.x;
+    if (w.tile >= s.split_begin) return false;
+    w.kb0 = 0;
+    w.kb1 = s.kblocks;
+    w.unit = -1;
+    return true;
+  }
+  const int u = blockIdx.x + (i - s.full_rounds) * gridDim.x;
+  if (u >= s.units) return false;
+  w.tile = s.split_begin + u / s.splits;
+  w.kb0 = (u % s.splits) * s.kb_per_split;
+  w.kb1 = min(s.kblocks, w.kb0 + s.kb_per_split);
+  w.unit = u;
+  return true;
+}
+
+__device__ __forceinline__ void epilogue_bar_sync() {
+  asm volatile("bar.sync 1, 128;" ::: "memory");  // warps 2..5 only
+}
+
+__device__ __forceinline__ void st_global_v4(float* p, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
 template <typename T, int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmC, int M, int N, int K, uint32_t idesc) {
+                   const __grid_constant__ CUtensorMap tmC, int M, int N, int K, uint32_t idesc,
+                   TcSched sched) {
   using L = TcLayout<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
@@ -98,10 +149,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tiles_m = (M + kBM - 1) / kBM;
-  const int tiles_n = (N + BN - 1) / BN;
-  const int num_tiles = tiles_m * tiles_n;
-  const int kblocks = (K + kBK - 1) / kBK;
+  const int tiles_m = sched.tiles_m;
+  const int tiles_n = sched.tiles_n;
+  volatile int* last_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 8);
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmA);
@@ -135,10 +185,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      WorkItem w;
+      for (int i = 0; ok && work_item(sched, i, w); ++i) {
         int mb, nb;
-        tile_coords(tile, tiles_m, tiles_n, mb, nb);
-        for (int kb = 0; kb < kblocks; ++kb) {
+        tile_coords(w.tile, tiles_m, tiles_n, mb, nb);
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, wd, kWdProducer)) {
             ok = false;
             break;
@@ -177,14 +228,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      WorkItem w;
+      for (int i = 0; ok && work_item(sched, i, w); ++i) {
         if (!mbar_wait_bounded(tempty_bar(acc), acc_phase ^ 1u, abort_flag, wd, kWdMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_bounded(full_bar(stage), phase, abort_flag, wd, kWdMma)) {
             ok = false;
             break;
@@ -198,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // B: MN-major, advance 16 K rows (2 atoms of 8 rows x 128 B).
             const uint64_t ad = sdesc_sw128(a0 + k * kUmmaK * 2, 16, 1024);
             const uint64_t bd = sdesc_sw128(b0 + k * kUmmaK * 128, L::kBBox, 1024);
-            umma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0);
+            umma_f16(d_tmem, ad, bd, idesc, kb > w.kb0 || k > 0);
           }
           umma_commit(empty_bar(stage));
           if (++stage == STAGES) {
@@ -225,9 +277,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     int nstore = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    // Packs 64 fp32 values of this lane's row into 16-bit, stages them in a
+    // 128-byte-swizzled 32 x 64 box and TMA-stores the box at (x, y).
+    auto store_chunk = [&](const float (&f)[64], int x, int y) {
+      uint32_t pk[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) pk[i] = Elem<T>::pack2(f[2 * i], f[2 * i + 1]);
+      const uint32_t buf = cbuf + (nstore & 1) * L::kCBuf;
+      if (nstore >= 2 && lane == 0) bulk_wait_read<1>();
+      __syncwarp();
+      // Row `lane` of the box, 16-byte chunk j stored at j ^ (row % 8).
+      const uint32_t row = buf + lane * 128;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        st_shared_v4(row + ((j ^ (lane & 7)) << 4), pk[4 * j], pk[4 * j + 1], pk[4 * j + 2],
+                     pk[4 * j + 3]);
+      }
+      fence_proxy_async_shared();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(&tmC, buf, x, y);
+        bulk_commit();
+      }
+      ++nstore;
+    };
+    WorkItem w;
+    for (int i = 0; work_item(sched, i, w); ++i) {
       int mb, nb;
-      tile_coords(tile, tiles_m, tiles_n, mb, nb);
+      tile_coords(w.tile, tiles_m, tiles_n, mb, nb);
       int ok = 1;
       if (lane == 0) ok = mbar_wait_bounded(tfull_bar(acc), acc_phase, abort_flag, wd, kWdEpilogue);
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -235,6 +312,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t trow = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                             static_cast<uint32_t>(acc * BN);
+      const int row_in_tile = q * 32 + lane;
+      const int store_y = mb * kBM + q * 32;
 #pragma unroll 1
       for (int c = 0; c < BN / 64; ++c) {
         uint32_t r[64];
@@ -247,31 +326,58 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(tempty_bar(acc));
         }
+        if (w.unit >= 0) {
+          // K-split unit: keep the fp32 partial for the tile's last arriver.
+          float* dst = sched.ws + (static_cast<size_t>(w.unit) * kBM + row_in_tile) * BN + c * 64;
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            st_global_v4(dst + 4 * j, r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+          continue;
+        }
         const int store_x = nb * BN + c * 64;
-        const int store_y = mb * kBM + q * 32;
         if (store_x >= N || store_y >= M) continue;  // box entirely outside C
-        uint32_t pk[32];
+        float f[64];
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          pk[i] = Elem<T>::pack2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
-        const uint32_t buf = cbuf + (nstore & 1) * L::kCBuf;
-        if (nstore >= 2 && lane == 0) bulk_wait_read<1>();
-        __syncwarp();
-        // Row `lane` of the 32 x 64 box, 16-byte chunk j stored at j ^ (row % 8)
-        // (the 128-byte swizzle the store's tensor map expects).
-        const uint32_t row = buf + lane * 128;
+        for (int j = 0; j < 64; ++j) f[j] = __uint_as_float(r[j]);
+        store_chunk(f, store_x, store_y);
+      }
+      if (w.unit >= 0) {
+        // All four warps' partial rows are written; count this unit in.
+        __threadfence();
+        epilogue_bar_sync();
+        const int slot = w.tile - sched.split_begin;
+        if (warp == 2 && lane == 0) {
+          const unsigned prev = atomicAdd(&sched.counters[slot], 1u);
+          const bool last = prev == static_cast<unsigned>(sched.splits - 1);
+          if (last) sched.counters[slot] = 0u;  // ready for the next launch
+          *last_flag = last ? 1 : 0;
+        }
+        epilogue_bar_sync();
+        if (*last_flag) {
+          __threadfence();
+          const int first_unit = slot * sched.splits;
+#pragma unroll 1
+          for (int c = 0; c < BN / 64; ++c) {
+            float acc_f[64];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          st_shared_v4(row + ((j ^ (lane & 7)) << 4), pk[4 * j], pk[4 * j + 1], pk[4 * j + 2],
-                       pk[4 * j + 3]);
+            for (int j = 0; j < 64; ++j) acc_f[j] = 0.0f;
+            for (int sp = 0; sp < sched.splits; ++sp) {
+              const float* src = sched.ws +
+                  (static_cast<size_t>(first_unit + sp) * kBM + row_in_tile) * BN + c * 64;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(src) + j);
+                acc_f[4 * j] += v.x;
+                acc_f[4 * j + 1] += v.y;
+                acc_f[4 * j + 2] += v.z;
+                acc_f[4 * j + 3] += v.w;
+              }
+            }
+            const int store_x = nb * BN + c * 64;
+            if (store_x >= N || store_y >= M) continue;
+            store_chunk(acc_f, store_x, store_y);
+          }
         }
-        fence_proxy_async_shared();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&tmC, buf, store_x, store_y);
-          bulk_commit();
-        }
-        ++nstore;
       }
       if (++acc == 2) {
         acc = 0;
@@ -290,35 +396,106 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+struct TcPlan {
+  int grid;
+  TcSched sched;
+  size_t ws_bytes;       // 0: no K-split phase
+  size_t counter_bytes;  // leading part of the workspace holding the counters
+};
+
+// Tile schedule for the device: whole tiles round-robin, and - when a workspace
+// is available - the partial last wave cut into K splits over all SMs.  The
+// split count S minimises ceil(rem * S / sms) / S, the last phase's length in
+// tiles, with every split keeping >= 4 K blocks.
+TcPlan plan_tc(int M, int N, int K, int BN, int sms, bool allow_split) {
+  TcPlan p{};
+  TcSched& s = p.sched;
+  s.tiles_m = (M + kBM - 1) / kBM;
+  s.tiles_n = (N + BN - 1) / BN;
+  s.num_tiles = s.tiles_m * s.tiles_n;
+  s.kblocks = (K + kBK - 1) / kBK;
+  const int full = s.num_tiles / sms;
+  const int rem = s.num_tiles - full * sms;
+  int best_s = 1;
+  double best_cost = 1.0;
+  if (allow_split && full >= 1 && rem > 0) {
+    for (int S = 2; S <= 8; ++S) {
+      if (s.kblocks / S < 4) break;
+      const double cost = static_cast<double>((rem * S + sms - 1) / sms) / S + 0.03 * S / 8;
+      if (cost < best_cost - 1e-9) {
+        best_cost = cost;
+        best_s = S;
+      }
+    }
+  }
+  if (best_s == 1) {
+    p.grid = s.num_tiles < sms ? s.num_tiles : sms;
+    s.full_rounds = (s.num_tiles + p.grid - 1) / p.grid;
+    s.split_begin = s.num_tiles;
+    s.splits = 1;
+    s.kb_per_split = s.kblocks;
+    s.units = 0;
+    return p;
+  }
+  p.grid = sms;
+  s.full_rounds = full;
+  s.split_begin = full * sms;
+  s.kb_per_split = (s.kblocks + best_s - 1) / best_s;
+  s.splits = (s.kblocks + s.kb_per_split - 1) / s.kb_per_split;  // every split non-empty
+  s.units = rem * s.splits;
+  p.counter_bytes = (static_cast<size_t>(rem) * sizeof(unsigned) + 255) & ~static_cast<size_t>(255);
+  p.ws_bytes = p.counter_bytes + static_cast<size_t>(s.units) * kBM * BN * sizeof(float);
+  return p;
+}
+
 template <typename T, int BN, int STAGES>
 int launch_tc(void* c, const void* a, const void* b, int M, int N, int K, bool bf16,
-              cudaStream_t stream, const DeviceInfo& info) {
+              void* workspace, size_t ws_bytes, cudaStream_t stream, const DeviceInfo& info) {
   using L = TcLayout<BN, STAGES>;
   auto kernel = gemm_tc_kernel<T, BN, STAGES>;
   if (int st = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), L::kAlloc, info)) return st;
+  TcPlan p = plan_tc(M, N, K, BN, info.sm_count, workspace != nullptr);
+  if (p.ws_bytes > 0 && (ws_bytes < p.ws_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255)))
+    p = plan_tc(M, N, K, BN, info.sm_count, false);
+  if (p.ws_bytes > 0) {
+    p.sched.counters = static_cast<unsigned*>(workspace);
+    p.sched.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + p.counter_bytes);
+    cudaError_t e = cudaMemsetAsync(workspace, 0, p.counter_bytes, stream);
+    if (e != cudaSuccess)
+      return fail(AOTK_ERR_CUDA, "tcgen05 gemm: counter reset: %s", cudaGetErrorString(e));
+  }
   CUtensorMap ta, tb, tc;
   if (int st = make_tmap_2d_16bit(&ta, a, bf16, M, K, K, kBK, kBM)) return st;
   if (int st = make_tmap_2d_16bit(&tb, b, bf16, K, N, N, 64, kBK)) return st;
   if (int st = make_tmap_2d_16bit(&tc, c, bf16, M, N, N, 64, 32)) return st;
-  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
-  const int grid = tiles < info.sm_count ? tiles : info.sm_count;
   const uint32_t idesc = idesc_f16(bf16, kBM, BN, /*a_mn_major=*/false, /*b_mn_major=*/true);
-  kernel<<<grid, kThreads, L::kAlloc, stream>>>(ta, tb, tc, M, N, K, idesc);
+  kernel<<<p.grid, kThreads, L::kAlloc, stream>>>(ta, tb, tc, M, N, K, idesc, p.sched);
   return check_launch("tcgen05 gemm");
 }
 
+constexpr int kTcBN = 256;
+constexpr int kTcStages = 4;
+
 }  // namespace
 
+size_t gemm_tc_workspace_size(int64_t M, int64_t N, int64_t K, int sm_count) {
+  if (M <= 0 || N <= 0 || K <= 0 || M >= (1LL << 31) || N >= (1LL << 31) || K >= (1LL << 31))
+    return 0;
+  return plan_tc((int)M, (int)N, (int)K, kTcBN, sm_count, true).ws_bytes;
+}
+
 int gemm_tc(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K, int dtype,
-            void* stream) {
+            void* workspace, size_t ws_bytes, void* stream) {
   DeviceInfo info;
   if (int st = current_device_info(&info)) return st;
   if (int st = require_sm100(info)) return st;
   if (int st = check_tc_preconditions("aotk_gemm_tc", c, a, b, M, N, K, dtype)) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int m = (int)M, n = (int)N, k = (int)K;
-  if (dtype == AOTK_BFLOAT16) return launch_tc<__nv_bfloat16, 256, 4>(c, a, b, m, n, k, true, s, info);
-  return launch_tc<__half, 256, 4>(c, a, b, m, n, k, false, s, info);
+  if (dtype == AOTK_BFLOAT16)
+    return launch_tc<__nv_bfloat16, kTcBN, kTcStages>(c, a, b, m, n, k, true, workspace, ws_bytes,
+                                                      s, info);
+  return launch_tc<__half, kTcBN, kTcStages>(c, a, b, m, n, k, false, workspace, ws_bytes, s, info);
 }
 
 int tc_watchdog(uint32_t* status, bool clear) {

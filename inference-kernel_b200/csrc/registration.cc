@@ -161,8 +161,16 @@ void gemm_opt(at::Tensor out, at::Tensor a, at::Tensor b) {
   const char* op = "gemm_opt";
   const GemmArgs g = check_gemm(out, a, b, op);
   c10::cuda::CUDAGuard guard(a.device());
-  check_status(aotk_gemm_opt(out.data_ptr(), a.data_ptr(), b.data_ptr(), g.M, g.N, g.K, g.dtype,
-                             current_stream(a)),
+  size_t ws_bytes = 0;
+  check_status(aotk_gemm_opt_workspace_size(g.M, g.N, g.K, g.dtype, &ws_bytes), op);
+  // Scratch for the K-split last wave comes from torch's caching allocator
+  // (stream-ordered, so reuse by the next call on this stream is safe).
+  at::Tensor ws;
+  if (ws_bytes > 0)
+    ws = at::empty({static_cast<int64_t>(ws_bytes)}, a.options().dtype(at::kByte));
+  check_status(aotk_gemm_opt_ws(out.data_ptr(), a.data_ptr(), b.data_ptr(), g.M, g.N, g.K, g.dtype,
+                                ws_bytes > 0 ? ws.data_ptr() : nullptr, ws_bytes,
+                                current_stream(a)),
                op);
 }
 

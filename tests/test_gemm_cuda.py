@@ -184,3 +184,55 @@ def test_full_size_sampled_rows(shape):
     rows = np.unique(np.random.default_rng(0).integers(0, M, size=min(M, 48)))
     expect = ops.gemm(a[rows], b, "bfloat16")
     assert_close_for_gemm(got[torch.as_tensor(rows, device="cuda")], expect, "bfloat16")
+
+
+# ---- K-split last wave (aotk_gemm_opt_ws) ----
+
+SPLIT_SHAPES = [(2560, 1024, 2048), (2560, 2048, 2048), (4096, 4096, 4096), (4096, 8192, 7168)]
+
+
+@pytest.mark.parametrize("shape", SPLIT_SHAPES, ids=str)
+def test_split_last_wave_matches_oracle(shape):
+    """Shapes whose tile count leaves a partial last wave: the leftover tiles
+    are computed in K splits through a workspace and must match the oracle,
+    be bit-identical across calls, and not depend on the workspace contents."""
+    import torch
+
+    from aot_kernel import capi
+
+    M, K, N = shape
+    a, b = _inputs(M, K, N, "bfloat16", seed=M + 3 * N, b_std=K ** -0.5)
+    ta, tb = to_device(a, "bfloat16"), to_device(b, "bfloat16")
+    ws_bytes = capi.gemm_opt_workspace_size(M, N, K, capi.BFLOAT16)
+    assert ws_bytes > 0, "shape expected to use the split schedule"
+    ws = torch.full((ws_bytes,), 0xAB, dtype=torch.uint8, device="cuda")  # garbage on purpose
+    outs = []
+    for _ in range(2):
+        c = torch.empty((M, N), device="cuda", dtype=torch.bfloat16)
+        capi.gemm_opt_ws(c, ta, tb, M, N, K, capi.BFLOAT16, ws, ws_bytes)
+        outs.append(c)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+    rows = np.unique(np.random.default_rng(1).integers(0, M, size=64))
+    # the split tiles are the last ones in raster order: check the last 128-row block too
+    rows = np.unique(np.concatenate([rows, np.arange(M - 128, M, 7)]))
+    expect = ops.gemm(a[rows], b, "bfloat16")
+    assert_close_for_gemm(outs[0][torch.as_tensor(rows, device="cuda")], expect, "bfloat16")
+    assert capi.watchdog_status() == 0
+
+
+def test_split_and_whole_schedules_agree():
+    import torch
+
+    import aot_kernel
+    from aot_kernel import capi
+
+    M, K, N = 4096, 4096, 4096
+    a, b = _inputs(M, K, N, "bfloat16", seed=77, b_std=K ** -0.5)
+    ta, tb = to_device(a, "bfloat16"), to_device(b, "bfloat16")
+    whole = torch.empty((M, N), device="cuda", dtype=torch.bfloat16)
+    capi.gemm_tc(whole, ta, tb, M, N, K, capi.BFLOAT16)
+    split = aot_kernel.gemm(ta, tb)  # the op allocates the workspace
+    torch.cuda.synchronize()
+    diff = (whole.float() - split.float()).abs().max().item()
+    assert diff <= 2e-2 * whole.float().abs().max().item()
