@@ -47,6 +47,7 @@ constexpr int kBK = 64;  // one 128-byte swizzle row of 16-bit elements
 constexpr int kUmmaK = 16;
 constexpr int kThreads = 192;
 constexpr int kGroupM = 16;  // M tiles per raster group
+constexpr int kMaxSplits = 4;
 
 enum : unsigned { kWdProducer = 1u, kWdMma = 2u, kWdEpilogue = 4u };
 
@@ -127,8 +128,8 @@ __device__ __forceinline__ void st_global_v4(float* p, uint32_t a, uint32_t b, u
 template <typename T, int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmC, int M, int N, int K, uint32_t idesc,
-                   TcSched sched) {
+                   const __grid_constant__ CUtensorMap tmC, T* __restrict__ C, int M, int N, int K,
+                   uint32_t idesc, TcSched sched) {
   using L = TcLayout<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
@@ -354,28 +355,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         epilogue_bar_sync();
         if (*last_flag) {
+          // Sum the S partial tiles (split order) and store the 16-bit tile.
+          // The 128 epilogue threads sweep the tile in float4 steps, so loads
+          // and stores are coalesced along rows.
           __threadfence();
-          const int first_unit = slot * sched.splits;
+          const int et = threadIdx.x - 64;  // 0..127
+          const size_t unit_stride = static_cast<size_t>(kBM) * BN;
+          const float* base = sched.ws + static_cast<size_t>(slot * sched.splits) * unit_stride;
+          constexpr int kF4 = kBM * BN / 4;
 #pragma unroll 1
-          for (int c = 0; c < BN / 64; ++c) {
-            float acc_f[64];
+          for (int f0 = et; f0 < kF4; f0 += 4 * 128) {
+            float4 sum[4];
 #pragma unroll
-            for (int j = 0; j < 64; ++j) acc_f[j] = 0.0f;
+            for (int u = 0; u < 4; ++u) sum[u] = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int sp = 0; sp < sched.splits; ++sp) {
-              const float* src = sched.ws +
-                  (static_cast<size_t>(first_unit + sp) * kBM + row_in_tile) * BN + c * 64;
+              float4 v[4];
 #pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                const float4 v = __ldcg(reinterpret_cast<const float4*>(src) + j);
-                acc_f[4 * j] += v.x;
-                acc_f[4 * j + 1] += v.y;
-                acc_f[4 * j + 2] += v.z;
-                acc_f[4 * j + 3] += v.w;
+              for (int u = 0; u < 4; ++u)
+                v[u] = __ldcg(reinterpret_cast<const float4*>(base + sp * unit_stride) + f0 + u * 128);
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                sum[u].x += v[u].x;
+                sum[u].y += v[u].y;
+                sum[u].z += v[u].z;
+                sum[u].w += v[u].w;
               }
             }
-            const int store_x = nb * BN + c * 64;
-            if (store_x >= N || store_y >= M) continue;
-            store_chunk(acc_f, store_x, store_y);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int f = f0 + u * 128;
+              const int gr = mb * kBM + f / (BN / 4);
+              const int gc = nb * BN + (f % (BN / 4)) * 4;
+              if (gr < M && gc < N) {  // N % 8 == 0: gc < N implies gc + 3 < N
+                uint2 o;
+                o.x = Elem<T>::pack2(sum[u].x, sum[u].y);
+                o.y = Elem<T>::pack2(sum[u].z, sum[u].w);
+                *reinterpret_cast<uint2*>(C + static_cast<size_t>(gr) * N + gc) = o;
+              }
+            }
           }
         }
       }
@@ -403,10 +420,11 @@ struct TcPlan {
   size_t counter_bytes;  // leading part of the workspace holding the counters
 };
 
-// Tile schedule for the device: whole tiles round-robin, and - when a workspace
-// is available - the partial last wave cut into K splits over all SMs.  The
-// split count S minimises ceil(rem * S / sms) / S, the last phase's length in
-// tiles, with every split keeping >= 4 K blocks.
+// Tile schedule for the device: whole tiles round-robin and - when a
+// workspace is available and the tile count leaves a partial last wave of
+// `rem` tiles - those tiles cut into S = min(4, sms / rem, kblocks / 4) K
+// splits, so the split units form one round over the SMs and the last wave
+// lasts about 1/S of a tile plus the partial-sum pass.
 TcPlan plan_tc(int M, int N, int K, int BN, int sms, bool allow_split) {
   TcPlan p{};
   TcSched& s = p.sched;
@@ -416,19 +434,14 @@ TcPlan plan_tc(int M, int N, int K, int BN, int sms, bool allow_split) {
   s.kblocks = (K + kBK - 1) / kBK;
   const int full = s.num_tiles / sms;
   const int rem = s.num_tiles - full * sms;
-  int best_s = 1;
-  double best_cost = 1.0;
+  int S = 1;
   if (allow_split && full >= 1 && rem > 0) {
-    for (int S = 2; S <= 8; ++S) {
-      if (s.kblocks / S < 4) break;
-      const double cost = static_cast<double>((rem * S + sms - 1) / sms) / S + 0.03 * S / 8;
-      if (cost < best_cost - 1e-9) {
-        best_cost = cost;
-        best_s = S;
-      }
-    }
+    S = kMaxSplits;
+    if (S > sms / rem) S = sms / rem;
+    if (S > s.kblocks / 4) S = s.kblocks / 4;
+    if (S < 1) S = 1;
   }
-  if (best_s == 1) {
+  if (S == 1) {
     p.grid = s.num_tiles < sms ? s.num_tiles : sms;
     s.full_rounds = (s.num_tiles + p.grid - 1) / p.grid;
     s.split_begin = s.num_tiles;
@@ -440,7 +453,7 @@ TcPlan plan_tc(int M, int N, int K, int BN, int sms, bool allow_split) {
   p.grid = sms;
   s.full_rounds = full;
   s.split_begin = full * sms;
-  s.kb_per_split = (s.kblocks + best_s - 1) / best_s;
+  s.kb_per_split = (s.kblocks + S - 1) / S;
   s.splits = (s.kblocks + s.kb_per_split - 1) / s.kb_per_split;  // every split non-empty
   s.units = rem * s.splits;
   p.counter_bytes = (static_cast<size_t>(rem) * sizeof(unsigned) + 255) & ~static_cast<size_t>(255);
@@ -469,7 +482,8 @@ int launch_tc(void* c, const void* a, const void* b, int M, int N, int K, bool b
   if (int st = make_tmap_2d_16bit(&tb, b, bf16, K, N, N, 64, kBK)) return st;
   if (int st = make_tmap_2d_16bit(&tc, c, bf16, M, N, N, 64, 32)) return st;
   const uint32_t idesc = idesc_f16(bf16, kBM, BN, /*a_mn_major=*/false, /*b_mn_major=*/true);
-  kernel<<<p.grid, kThreads, L::kAlloc, stream>>>(ta, tb, tc, M, N, K, idesc, p.sched);
+  kernel<<<p.grid, kThreads, L::kAlloc, stream>>>(ta, tb, tc, static_cast<T*>(c), M, N, K, idesc,
+                                                  p.sched);
   return check_launch("tcgen05 gemm");
 }
 
