@@ -115,6 +115,23 @@ AOTK_API int aotk_gemm_opt_ws(void* c, const void* a, const void* b, int64_t M, 
 AOTK_API int aotk_gemm_opt_workspace_size(int64_t M, int64_t N, int64_t K, int dtype,
                                           size_t* bytes);
 
+/* aotk_gemm_opt_ws for callers that cannot allocate device memory: hosts that
+ * reach this library only through its C ABI (an FFI plugin with no CUDA
+ * allocator of its own) and serving loops that must not call cudaMalloc,
+ * which can synchronise the device.  The K-split scratch comes from a 24 MiB
+ * array compiled into the library (device global memory, held on every GPU
+ * where the library's kernels are loaded until the process exits).  The
+ * entry point calls no cudaMalloc, cudaFree or allocating library routine.
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress, once per device); make that first call before any
+ * stream capture.  Every call on a device shares the one array and resets the
+ * part it needs, so calls whose kernels overlap on the GPU (different streams
+ * without ordering) race and corrupt each other's results; order them on one
+ * stream.  Problems needing more scratch than the array holds return
+ * AOTK_ERR_UNSUPPORTED.  No counterpart in the reference. */
+AOTK_API int aotk_gemm_opt_noalloc(void* c, const void* a, const void* b, int64_t M, int64_t N,
+                                   int64_t K, int dtype, void* stream);
+
 /* Any-dtype, any-shape GEMM (SIMT, fp32 accumulation).
  * Replaces gemm(Tensor! out, Tensor a, Tensor b)
  * (aot_kernel/csrc/gemm/gemm.cu:106-157, registration.cc:20-21). */

@@ -32,6 +32,7 @@ SIGNATURES: dict[str, list] = {
     "aotk_gemm_opt": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
     "aotk_gemm_opt_ws": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr, ctypes.c_size_t, _ptr],
     "aotk_gemm_opt_workspace_size": [_i64, _i64, _i64, _int, ctypes.POINTER(ctypes.c_size_t)],
+    "aotk_gemm_opt_noalloc": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
     "aotk_gemm": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
     "aotk_gemm_tc": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
     "aotk_gemm_skinny": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
@@ -136,6 +137,11 @@ def gemm_opt_workspace_size(M, N, K, dtype) -> int:
 def gemm_opt_ws(c, a, b, M, N, K, dtype, workspace, workspace_bytes, stream=None) -> None:
     _call("aotk_gemm_opt_ws", _p(c), _p(a), _p(b), M, N, K, dtype, _p(workspace), workspace_bytes,
           _stream(stream))
+
+
+def gemm_opt_noalloc(c, a, b, M, N, K, dtype, stream=None) -> None:
+    """aotk_gemm_opt_ws with the library's built-in scratch; allocates nothing."""
+    _gemm("aotk_gemm_opt_noalloc", c, a, b, M, N, K, dtype, stream)
 
 
 def gemm(c, a, b, M, N, K, dtype, stream=None) -> None:

@@ -1,0 +1,46 @@
+"""aotk_gemm_opt_noalloc: the GEMM entry point for callers that cannot
+allocate device memory (an FFI host with no CUDA allocator of its own, or a
+serving loop that must not call cudaMalloc).  Its K-split scratch is a static
+array inside libaotk.so.  Checked through the C ABI against aotk_gemm_opt_ws
+with a caller-allocated workspace, on two calls in a row.  Kept in its own
+file, named to be collected last."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from tests.conftest import assert_close_for_gemm, to_device
+from oracle.inputs import randn
+
+pytestmark = pytest.mark.gpu
+
+# (M, K, N): the first two leave a partial last wave on a 148-SM B200 and use
+# the scratch; the last needs none (whole tiles only).
+SHAPES = [(4096, 4096, 4096), (2560, 2048, 2048), (8192, 1024, 8192)]
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=str)
+def test_noalloc_matches_workspace_entry_point(shape):
+    import torch
+
+    from aot_kernel import capi
+
+    M, K, N = shape
+    a = to_device(randn((M, K), 900 + M, "bfloat16"), "bfloat16")
+    b = to_device(randn((K, N), 901 + N, "bfloat16", std=K ** -0.5), "bfloat16")
+    ws_bytes = capi.gemm_opt_workspace_size(M, N, K, capi.BFLOAT16)
+    ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device="cuda")
+    ref = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    capi.gemm_opt_ws(ref, a, b, M, N, K, capi.BFLOAT16, ws, ws_bytes)
+    outs = []
+    for _ in range(2):  # two calls in a row share the static scratch
+        c = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
+        capi.gemm_opt_noalloc(c, a, b, M, N, K, capi.BFLOAT16)
+        outs.append(c)
+    torch.cuda.synchronize()
+    for c in outs:
+        assert not torch.isnan(c).any()
+        assert_close_for_gemm(c, ref, "bfloat16")
+    assert capi.watchdog_status() == 0
+
