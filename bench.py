@@ -73,6 +73,8 @@ def parse_args():
     ap.add_argument("--no-tp", action="store_true", help="skip the tensor-parallel MLP block")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--tp-chunks", type=int, default=1)
+    ap.add_argument("--tp-allreduce", choices=["nccl", "fused"], default="fused",
+                    help="down projection + all-reduce: NCCL after the GEMM, or one fused kernel")
     ap.add_argument("--case", choices=sorted(CASES), default=None,
                     help="run only this workload's launches (for profilers)")
     return ap.parse_args()
@@ -396,7 +398,9 @@ def tp_mlp(args, rank: int, world: int, peaks: dict) -> dict:
     wd_r = shard_down(w_d, rank, world)
     del w_d
     torch.cuda.empty_cache()
-    block = TensorParallelMLP(MLPShard(nw, wgu_r, wd_r), eps=1e-6, chunks=args.tp_chunks)
+    allreduce = args.tp_allreduce if world > 1 else "nccl"
+    block = TensorParallelMLP(MLPShard(nw, wgu_r, wd_r), eps=1e-6, chunks=args.tp_chunks,
+                              allreduce=allreduce)
     for _ in range(max(3, args.warmup)):
         block(x)
     torch.cuda.synchronize()
@@ -419,25 +423,30 @@ def tp_mlp(args, rank: int, world: int, peaks: dict) -> dict:
     per_gpu_ideal_ms = flops / world / (peaks["bf16_tflops"] * 1e12) * 1e3
     return {"tokens_per_s": T / (ms * 1e-3), "ms_per_step": ms, "tokens": T, "hidden": H,
             "intermediate": inter, "tp": world, "chunks": args.tp_chunks,
-            "gpu_launches_per_step": 5 if world == 1 else 4 + args.tp_chunks,
+            "allreduce": allreduce if world > 1 else None,
+            "gpu_launches_per_step": 4 if world == 1 or allreduce == "fused" else 3 + args.tp_chunks,
             "tensor_frac_per_gpu": per_gpu_ideal_ms / ms, "allreduce_bytes": T * H * 2,
             "phases_ms": phases}
 
 
 def tp_phase_breakdown(block, x, world: int, reps: int = 5) -> dict:
-    """Device time of each op of one block step (mean of `reps` untimed-region
-    passes, CUDA events between ops, max over ranks)."""
+    """Device time of each op of one block step (mean of `reps` passes outside
+    the timed region, CUDA events between ops, max over ranks).  A sleep
+    kernel queued first keeps the host ahead so dispatch gaps are not timed."""
     import torch
     import torch.distributed as dist
 
     ops, s = block.ops, block.shard
-    names = ["rms_norm", "gemm_gate_up", "silu_mul", "gemm_down", "all_reduce"]
+    fused = world > 1 and block.allreduce == "fused"
+    names = ["rms_norm", "gemm_gate_up", "silu_mul"]
+    names += ["gemm_down+all_reduce (fused)"] if fused else ["gemm_down", "all_reduce"]
     acc = torch.zeros(len(names), dtype=torch.float64, device="cuda")
     for _ in range(reps):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
+        torch.cuda._sleep(2_000_000)
         ev[0].record()
         h = ops.rms_norm(x, s.norm_weight, block.eps)
         ev[1].record()
@@ -445,11 +454,15 @@ def tp_phase_breakdown(block, x, world: int, reps: int = 5) -> dict:
         ev[2].record()
         act = ops.silu_mul(gu[:, :block.inter_local], gu[:, block.inter_local:])
         ev[3].record()
-        out = ops.gemm(act, s.w_down)
-        ev[4].record()
-        if world > 1:
-            dist.all_reduce(out)
-        ev[5].record()
+        if fused:
+            block._fused(act, s.w_down)
+            ev[4].record()
+        else:
+            out = ops.gemm(act, s.w_down)
+            ev[4].record()
+            if world > 1:
+                dist.all_reduce(out)
+            ev[5].record()
         torch.cuda.synchronize()
         acc += torch.tensor([ev[i].elapsed_time(ev[i + 1]) for i in range(len(names))],
                             dtype=torch.float64, device="cuda")

@@ -154,6 +154,47 @@ AOTK_API int aotk_gemm_tc(void* c, const void* a, const void* b, int64_t M, int6
 AOTK_API int aotk_gemm_skinny(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
                      int dtype, void* stream);
 
+/* ---- gemm fused with the tensor-parallel all-reduce -------------------- */
+
+/* Buffers of one rank for aotk_gemm_allreduce.  `part` and the output are
+ * [M, N] row-major buffers of the GEMM's dtype allocated symmetrically on all
+ * ranks and bound to NVSwitch multicast objects (NVLS); the *_multicast
+ * fields are the multicast addresses of the two.  counters / done are
+ * zero-initialised uint32 words in memory every rank can access: counters
+ * needs aotk_gemm_allreduce_tiles(M, N) entries, done one; peer_counters[r]
+ * and peer_done[r] (device arrays of `world` pointers) are rank r's words as
+ * mapped on this GPU.  epoch is 1 on the first call and grows by 1 per call,
+ * identically on every rank. */
+typedef struct aotk_allreduce_buffers {
+  int rank;
+  int world;
+  void* part;
+  uint64_t part_multicast;
+  uint64_t out_multicast;
+  uint32_t* counters;
+  uint32_t* const* peer_counters;
+  uint32_t* done;
+  uint32_t* const* peer_done;
+  uint32_t epoch;
+} aotk_allreduce_buffers;
+
+/* Number of output tiles (arrival counters) of an [M, N] aotk_gemm_allreduce. */
+AOTK_API int aotk_gemm_allreduce_tiles(int64_t M, int64_t N, int64_t* tiles);
+
+/* out = sum over ranks of A_r[M, K] * B_r[K, N], on every rank of a
+ * tensor-parallel group (one process per GPU), in one kernel: each rank's
+ * persistent tcgen05 GEMM stores its partial tiles into `part`, and as the
+ * W partials of a tile arrive, the tile's owner rank (tile % W) sums them
+ * through the switch (multimem.ld_reduce, fp32 accumulation) and writes the
+ * 16-bit result into every rank's output (multimem.st), overlapping the
+ * transfer with the rest of the GEMM.  FLOAT16/BFLOAT16, K % 8 == 0,
+ * N % 8 == 0.  All ranks must call with the same M, N, K, dtype and epoch;
+ * every wait is bounded (~1 s) and a timeout sets watchdog bit 64.
+ * Replaces the down projection + NCCL all-reduce of the tensor-parallel MLP
+ * block (no reference counterpart: the reference has no multi-GPU code). */
+AOTK_API int aotk_gemm_allreduce(const void* a, const void* b, int64_t M, int64_t N, int64_t K,
+                                 int dtype, const aotk_allreduce_buffers* bufs, void* stream);
+
 /* Watchdog word of the tcgen05 kernels on `device`: a bit mask of pipeline
  * waits that gave up after their time limit (0 = healthy).  Synchronises the
  * device.  clear != 0 resets it to 0 after reading. */

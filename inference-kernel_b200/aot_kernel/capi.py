@@ -37,7 +37,26 @@ SIGNATURES: dict[str, list] = {
     "aotk_gemm_tc": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
     "aotk_gemm_skinny": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
     "aotk_watchdog_status": [_int, ctypes.POINTER(ctypes.c_uint32), _int],
+    "aotk_gemm_allreduce_tiles": [_i64, _i64, ctypes.POINTER(ctypes.c_int64)],
+    "aotk_gemm_allreduce": [_ptr, _ptr, _i64, _i64, _i64, _int, ctypes.c_void_p, _ptr],
 }
+
+
+class AllReduceBuffers(ctypes.Structure):
+    """aotk_allreduce_buffers (include/aotk.h)."""
+
+    _fields_ = [
+        ("rank", ctypes.c_int),
+        ("world", ctypes.c_int),
+        ("part", ctypes.c_void_p),
+        ("part_multicast", ctypes.c_uint64),
+        ("out_multicast", ctypes.c_uint64),
+        ("counters", ctypes.c_void_p),
+        ("peer_counters", ctypes.c_void_p),
+        ("done", ctypes.c_void_p),
+        ("peer_done", ctypes.c_void_p),
+        ("epoch", ctypes.c_uint32),
+    ]
 
 
 class AotkError(RuntimeError):
@@ -154,6 +173,17 @@ def gemm_tc(c, a, b, M, N, K, dtype, stream=None) -> None:
 
 def gemm_skinny(c, a, b, M, N, K, dtype, stream=None) -> None:
     _gemm("aotk_gemm_skinny", c, a, b, M, N, K, dtype, stream)
+
+
+def gemm_allreduce_tiles(M: int, N: int) -> int:
+    n = ctypes.c_int64(0)
+    _call("aotk_gemm_allreduce_tiles", M, N, ctypes.byref(n))
+    return n.value
+
+
+def gemm_allreduce(a, b, M, N, K, dtype, bufs: AllReduceBuffers, stream=None) -> None:
+    _call("aotk_gemm_allreduce", _p(a), _p(b), M, N, K, dtype, ctypes.addressof(bufs),
+          _stream(stream))
 
 
 def watchdog_status(device: int = 0, clear: bool = True) -> int:

@@ -9,7 +9,9 @@ same rows of W_down ([I/W, H]).  rms_norm and silu_mul are local; the only
 exchange is one all-reduce (sum) of the [T, H] partial outputs over NCCL.
 With ``chunks > 1`` the token dimension is cut into slices whose all-reduce
 (asynchronous, on NCCL's stream) overlaps the down projection of the next
-slice.
+slice.  With ``allreduce="fused"`` the down projection and the all-reduce are
+one kernel (``aotk_gemm_allreduce``): partial tiles are summed through
+NVSwitch multicast memory while the rest of the GEMM runs.
 
 The reference has no multi-GPU code; its oracle for this block is the
 unsharded composition of ref.rmsnorm, ref.gemm and ref.silu.
@@ -50,6 +52,61 @@ def shard_down(w_down: torch.Tensor, rank: int, world: int) -> torch.Tensor:
     return w_down[rank * s:(rank + 1) * s].contiguous()
 
 
+class FusedDownAllReduce:
+    """Symmetric buffers and call state of ``aotk_gemm_allreduce`` for one
+    [tokens, hidden] output on one process group.
+
+    ``part`` and ``out`` are allocated with torch's symmetric memory and bound
+    to NVSwitch multicast objects; the arrival counters and the done word live
+    in one zero-initialised symmetric int32 buffer.  The returned output is
+    ``out`` itself and is overwritten by the next call.
+    """
+
+    def __init__(self, tokens: int, hidden: int, dtype, device, group=None):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from . import capi
+
+        self.capi = capi
+        self.group = group or dist.group.WORLD
+        self.rank = dist.get_rank(self.group)
+        self.world = dist.get_world_size(self.group)
+        self.M, self.N = tokens, hidden
+        self.dtype = dtype
+        self.tiles = capi.gemm_allreduce_tiles(tokens, hidden)
+        self.part = symm_mem.empty((tokens, hidden), dtype=dtype, device=device)
+        self.out = symm_mem.empty((tokens, hidden), dtype=dtype, device=device)
+        self.sig = symm_mem.empty((self.tiles + 64,), dtype=torch.int32, device=device)
+        self.sig.zero_()
+        torch.cuda.synchronize(device)
+        hp = symm_mem.rendezvous(self.part, self.group)
+        ho = symm_mem.rendezvous(self.out, self.group)
+        hs = symm_mem.rendezvous(self.sig, self.group)
+        if not hp.multicast_ptr or not ho.multicast_ptr:
+            raise RuntimeError("NVSwitch multicast (NVLS) is not available on this group")
+        self._handles = (hp, ho, hs)
+        done_off = self.tiles * 4
+        self.peer_counters = torch.tensor(list(hs.buffer_ptrs), dtype=torch.int64, device=device)
+        self.peer_done = torch.tensor([p + done_off for p in hs.buffer_ptrs], dtype=torch.int64,
+                                      device=device)
+        self.epoch = 0
+        self.bufs = capi.AllReduceBuffers(
+            rank=self.rank, world=self.world, part=self.part.data_ptr(),
+            part_multicast=hp.multicast_ptr, out_multicast=ho.multicast_ptr,
+            counters=self.sig.data_ptr(), peer_counters=self.peer_counters.data_ptr(),
+            done=self.sig.data_ptr() + done_off, peer_done=self.peer_done.data_ptr(), epoch=0)
+        dist.barrier(self.group)  # every rank's counters are zero before the first call
+
+    def __call__(self, act: torch.Tensor, w_down: torch.Tensor) -> torch.Tensor:
+        if act.shape[0] != self.M or w_down.shape[1] != self.N or act.dtype != self.dtype:
+            raise ValueError("shape/dtype differs from the one the buffers were built for")
+        self.epoch += 1
+        self.bufs.epoch = self.epoch
+        self.capi.gemm_allreduce(act, w_down, self.M, self.N, act.shape[1],
+                                 self.capi.dtype_code(act.dtype), self.bufs)
+        return self.out
+
+
 @dataclass
 class MLPShard:
     norm_weight: torch.Tensor  # [H]
@@ -59,7 +116,7 @@ class MLPShard:
 
 class TensorParallelMLP:
     def __init__(self, shard: MLPShard, group=None, eps: float = 1e-6, chunks: int = 1,
-                 ops: SimpleNamespace | None = None):
+                 ops: SimpleNamespace | None = None, allreduce: str = "nccl"):
         self.shard = shard
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -69,6 +126,10 @@ class TensorParallelMLP:
         self.inter_local = shard.w_down.shape[0]
         if shard.w_gate_up.shape[1] != 2 * self.inter_local:
             raise ValueError("gate/up shard must be [H, 2 * I_local]")
+        if allreduce not in ("nccl", "fused"):
+            raise ValueError(f"allreduce must be 'nccl' or 'fused', got {allreduce!r}")
+        self.allreduce = allreduce
+        self._fused: FusedDownAllReduce | None = None
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         ops, s = self.ops, self.shard
@@ -77,6 +138,11 @@ class TensorParallelMLP:
         act = ops.silu_mul(gu[:, :self.inter_local], gu[:, self.inter_local:])
         if self.world == 1:
             return ops.gemm(act, s.w_down)
+        if self.allreduce == "fused":
+            if self._fused is None or self._fused.M != act.shape[0]:
+                self._fused = FusedDownAllReduce(act.shape[0], s.w_down.shape[1], act.dtype,
+                                                 act.device, self.group)
+            return self._fused(act, s.w_down)
         if self.chunks == 1:
             out = ops.gemm(act, s.w_down)
             dist.all_reduce(out, op=dist.ReduceOp.SUM, group=self.group)

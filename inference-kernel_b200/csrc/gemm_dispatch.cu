@@ -143,6 +143,19 @@ extern "C" int aotk_gemm_skinny(void* c, const void* a, const void* b, int64_t M
   return aotk::gemm_skinny(c, a, b, M, N, K, dtype, stream);
 }
 
+extern "C" int aotk_gemm_allreduce_tiles(int64_t M, int64_t N, int64_t* tiles) {
+  using namespace aotk;
+  if (!tiles || M < 0 || N < 0)
+    return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_gemm_allreduce_tiles: bad arguments");
+  *tiles = gemm_allreduce_tiles(M, N);
+  return AOTK_OK;
+}
+
+extern "C" int aotk_gemm_allreduce(const void* a, const void* b, int64_t M, int64_t N, int64_t K,
+                                   int dtype, const aotk_allreduce_buffers* bufs, void* stream) {
+  return aotk::gemm_allreduce(a, b, M, N, K, dtype, bufs, stream);
+}
+
 extern "C" int aotk_watchdog_status(int device, uint32_t* status, int clear) {
   using namespace aotk;
   if (!status) return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_watchdog_status: null pointer");

@@ -14,6 +14,12 @@ int gemm_tc(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t
             void* workspace, size_t ws_bytes, void* stream);
 size_t gemm_tc_workspace_size(int64_t M, int64_t N, int64_t K, int sm_count);
 
+// Persistent tcgen05 GEMM fused with an all-reduce of C over NVSwitch
+// multicast memory (gemm_tc.cu).
+int gemm_allreduce(const void* a, const void* b, int64_t M, int64_t N, int64_t K, int dtype,
+                   const aotk_allreduce_buffers* bufs, void* stream);
+int gemm_allreduce_tiles(int64_t M, int64_t N);
+
 // Swap-AB split-K tcgen05 kernel for M <= kSkinnyMaxM (gemm_skinny.cu).
 constexpr int64_t kSkinnyMaxM = 128;
 int gemm_skinny(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K, int dtype,

@@ -35,6 +35,8 @@
 #include "tmap.h"
 #include "vec.cuh"
 
+#include <type_traits>
+
 namespace aotk {
 namespace {
 
@@ -45,11 +47,12 @@ __device__ unsigned g_tc_watchdog;
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // one 128-byte swizzle row of 16-bit elements
 constexpr int kUmmaK = 16;
-constexpr int kThreads = 192;
+constexpr int kThreads = 192;       // plain GEMM: producer, MMA, 4 epilogue warps
+constexpr int kThreadsFused = 320;  // + 4 all-reduce warps (gemm_allreduce)
 constexpr int kGroupM = 16;  // M tiles per raster group
 constexpr int kMaxSplits = 4;
 
-enum : unsigned { kWdProducer = 1u, kWdMma = 2u, kWdEpilogue = 4u };
+enum : unsigned { kWdProducer = 1u, kWdMma = 2u, kWdEpilogue = 4u, kWdPeer = 64u };
 
 template <int BN, int STAGES>
 struct TcLayout {
@@ -125,11 +128,78 @@ __device__ __forceinline__ void st_global_v4(float* p, uint32_t a, uint32_t b, u
                : "memory");
 }
 
-template <typename T, int BN, int STAGES>
-__global__ void __launch_bounds__(kThreads, 1)
+// Fused all-reduce of the output over W ranks (one process per GPU) through
+// NVSwitch multicast memory.  Each rank stores its partial tile into its own
+// `part` buffer, then bumps the tile's arrival counter on the owner rank
+// (tile % W).  The owner's all-reduce warps wait until all W partials of the
+// tile have arrived, read their sum through the multicast address of `part`
+// (multimem.ld_reduce, fp32 accumulation) and write it to every rank's `out`
+// through the multicast address of `out` (multimem.st).  Counters only grow:
+// call number e (epoch, from 1) waits for W*e arrivals.  A final done
+// counter per rank (W * grid * e) tells each rank when every owner has
+// written its tiles.
+struct ArParams {
+  int rank, world;
+  uint64_t part_mc, out_mc;        // multicast addresses of part / out
+  unsigned* counters;              // this rank's per-tile arrival counters
+  unsigned* const* peer_counters;  // [world] each rank's counters (peer-mapped)
+  unsigned* done;                  // this rank's done counter
+  unsigned* const* peer_done;      // [world] each rank's done counter
+  unsigned epoch;
+};
+
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void red_release_sys_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void comm_bar_sync() {
+  asm volatile("bar.sync 2, 128;" ::: "memory");  // warps 6..9 only
+}
+// Waits until *p >= target; bounded like the pipeline waits.
+__device__ __forceinline__ bool wait_at_least(const unsigned* p, unsigned target,
+                                              volatile int* abort, unsigned* status) {
+  const long long t0 = clock64();
+  while (static_cast<int>(ld_acquire_sys(p) - target) < 0) {
+    if (*abort) return false;
+    if (clock64() - t0 > kWaitLimitCycles) {
+      *abort = 1;
+      atomicOr(status, kWdPeer);
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ void ld_reduce_bf16x8(uint64_t mc, uint4& v) {
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(mc)
+               : "memory");
+}
+__device__ __forceinline__ void ld_reduce_f16x8(uint64_t mc, uint4& v) {
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.f16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(mc)
+               : "memory");
+}
+__device__ __forceinline__ void multimem_st16(uint64_t mc, const uint4& v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x),
+               "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+template <typename T, int BN, int STAGES, bool kFused>
+__global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, T* __restrict__ C, int M, int N, int K,
-                   uint32_t idesc, TcSched sched) {
+                   uint32_t idesc, TcSched sched, ArParams ar) {
   using L = TcLayout<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
@@ -271,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_drain(drain_bar, 0);
     }
     __syncwarp();
-  } else {
+  } else if (warp < 6) {
     // ---------------- epilogue (warps 2..5) ----------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const uint32_t cbuf = sC + (warp - 2) * 2 * L::kCBuf;
@@ -327,13 +397,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(tempty_bar(acc));
         }
-        if (w.unit >= 0) {
-          // K-split unit: keep the fp32 partial for the tile's last arriver.
-          float* dst = sched.ws + (static_cast<size_t>(w.unit) * kBM + row_in_tile) * BN + c * 64;
+        if constexpr (!kFused) {
+          if (w.unit >= 0) {
+            // K-split unit: keep the fp32 partial for the tile's last arriver.
+            float* dst =
+                sched.ws + (static_cast<size_t>(w.unit) * kBM + row_in_tile) * BN + c * 64;
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            st_global_v4(dst + 4 * j, r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
-          continue;
+            for (int j = 0; j < 16; ++j)
+              st_global_v4(dst + 4 * j, r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+            continue;
+          }
         }
         const int store_x = nb * BN + c * 64;
         if (store_x >= N || store_y >= M) continue;  // box entirely outside C
@@ -342,55 +415,66 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < 64; ++j) f[j] = __uint_as_float(r[j]);
         store_chunk(f, store_x, store_y);
       }
-      if (w.unit >= 0) {
-        // All four warps' partial rows are written; count this unit in.
-        __threadfence();
+      if constexpr (kFused) {
+        // The partial tile is in `part` once this warp's stores complete;
+        // after all four epilogue warps, count it in on the tile's owner.
+        if (lane == 0) bulk_wait_all();
+        __syncwarp();
+        fence_proxy_async_global();
+        fence_sys();
         epilogue_bar_sync();
-        const int slot = w.tile - sched.split_begin;
-        if (warp == 2 && lane == 0) {
-          const unsigned prev = atomicAdd(&sched.counters[slot], 1u);
-          const bool last = prev == static_cast<unsigned>(sched.splits - 1);
-          if (last) sched.counters[slot] = 0u;  // ready for the next launch
-          *last_flag = last ? 1 : 0;
-        }
-        epilogue_bar_sync();
-        if (*last_flag) {
-          // Sum the S partial tiles (split order) and store the 16-bit tile.
-          // The 128 epilogue threads sweep the tile in float4 steps, so loads
-          // and stores are coalesced along rows.
+        if (warp == 2 && lane == 0) red_release_sys_add(ar.peer_counters[w.tile % ar.world] + w.tile, 1u);
+      } else {
+        if (w.unit >= 0) {
+          // All four warps' partial rows are written; count this unit in.
           __threadfence();
-          const int et = threadIdx.x - 64;  // 0..127
-          const size_t unit_stride = static_cast<size_t>(kBM) * BN;
-          const float* base = sched.ws + static_cast<size_t>(slot * sched.splits) * unit_stride;
-          constexpr int kF4 = kBM * BN / 4;
-#pragma unroll 1
-          for (int f0 = et; f0 < kF4; f0 += 4 * 128) {
-            float4 sum[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) sum[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int sp = 0; sp < sched.splits; ++sp) {
-              float4 v[4];
-#pragma unroll
-              for (int u = 0; u < 4; ++u)
-                v[u] = __ldcg(reinterpret_cast<const float4*>(base + sp * unit_stride) + f0 + u * 128);
-#pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                sum[u].x += v[u].x;
-                sum[u].y += v[u].y;
-                sum[u].z += v[u].z;
-                sum[u].w += v[u].w;
+          epilogue_bar_sync();
+          const int slot = w.tile - sched.split_begin;
+          if (warp == 2 && lane == 0) {
+            const unsigned prev = atomicAdd(&sched.counters[slot], 1u);
+            const bool last = prev == static_cast<unsigned>(sched.splits - 1);
+            if (last) sched.counters[slot] = 0u;  // ready for the next launch
+            *last_flag = last ? 1 : 0;
+          }
+          epilogue_bar_sync();
+          if (*last_flag) {
+            // Sum the S partial tiles (split order) and store the 16-bit tile.
+            // The 128 epilogue threads sweep the tile in float4 steps, so loads
+            // and stores are coalesced along rows.
+            __threadfence();
+            const int et = threadIdx.x - 64;  // 0..127
+            const size_t unit_stride = static_cast<size_t>(kBM) * BN;
+            const float* base = sched.ws + static_cast<size_t>(slot * sched.splits) * unit_stride;
+            constexpr int kF4 = kBM * BN / 4;
+  #pragma unroll 1
+            for (int f0 = et; f0 < kF4; f0 += 4 * 128) {
+              float4 sum[4];
+  #pragma unroll
+              for (int u = 0; u < 4; ++u) sum[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+              for (int sp = 0; sp < sched.splits; ++sp) {
+                float4 v[4];
+  #pragma unroll
+                for (int u = 0; u < 4; ++u)
+                  v[u] = __ldcg(reinterpret_cast<const float4*>(base + sp * unit_stride) + f0 + u * 128);
+  #pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  sum[u].x += v[u].x;
+                  sum[u].y += v[u].y;
+                  sum[u].z += v[u].z;
+                  sum[u].w += v[u].w;
+                }
               }
-            }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int f = f0 + u * 128;
-              const int gr = mb * kBM + f / (BN / 4);
-              const int gc = nb * BN + (f % (BN / 4)) * 4;
-              if (gr < M && gc < N) {  // N % 8 == 0: gc < N implies gc + 3 < N
-                uint2 o;
-                o.x = Elem<T>::pack2(sum[u].x, sum[u].y);
-                o.y = Elem<T>::pack2(sum[u].z, sum[u].w);
-                *reinterpret_cast<uint2*>(C + static_cast<size_t>(gr) * N + gc) = o;
+  #pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const int f = f0 + u * 128;
+                const int gr = mb * kBM + f / (BN / 4);
+                const int gc = nb * BN + (f % (BN / 4)) * 4;
+                if (gr < M && gc < N) {  // N % 8 == 0: gc < N implies gc + 3 < N
+                  uint2 o;
+                  o.x = Elem<T>::pack2(sum[u].x, sum[u].y);
+                  o.y = Elem<T>::pack2(sum[u].z, sum[u].w);
+                  *reinterpret_cast<uint2*>(C + static_cast<size_t>(gr) * N + gc) = o;
+                }
               }
             }
           }
@@ -403,6 +487,57 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (lane == 0) bulk_wait_all();
     __syncwarp();
+  } else if constexpr (kFused) {
+    // ---------------- all-reduce (warps 6..9) ----------------
+    // Same work list as the epilogue; for each tile this rank owns, wait for
+    // all W partials, then reduce through the switch and broadcast the sum.
+    const int ct = threadIdx.x - 192;  // 0..127
+    volatile int* peer_ok = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 12);
+    constexpr int kVecPerRow = BN * 2 / 16;
+    WorkItem w;
+    for (int i = 0; work_item(sched, i, w); ++i) {
+      if (w.tile % ar.world != ar.rank) continue;
+      if (ct == 0)
+        *peer_ok = wait_at_least(ar.counters + w.tile, ar.epoch * ar.world, abort_flag, wd) ? 1 : 0;
+      comm_bar_sync();
+      const bool ok = *peer_ok != 0;
+      comm_bar_sync();
+      if (!ok) break;
+      int mb, nb;
+      tile_coords(w.tile, tiles_m, tiles_n, mb, nb);
+#pragma unroll 1
+      for (int v0 = ct; v0 < kBM * kVecPerRow; v0 += 4 * 128) {
+        uint4 val[4];
+        uint64_t off[4];
+        bool live[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int v = v0 + u * 128;
+          const int gr = mb * kBM + v / kVecPerRow;
+          const int gc = nb * BN + (v % kVecPerRow) * 8;
+          live[u] = gr < M && gc < N;  // N % 8 == 0: the whole 16-byte vector is in range
+          off[u] = (static_cast<uint64_t>(gr) * N + gc) * sizeof(T);
+          if (live[u]) {
+            if constexpr (sizeof(T) == 2 && std::is_same<T, __nv_bfloat16>::value)
+              ld_reduce_bf16x8(ar.part_mc + off[u], val[u]);
+            else
+              ld_reduce_f16x8(ar.part_mc + off[u], val[u]);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (live[u]) multimem_st16(ar.out_mc + off[u], val[u]);
+      }
+    }
+    // Every owner on every rank has written its tiles once all W * grid CTAs
+    // have checked in on this rank.
+    fence_sys();
+    comm_bar_sync();
+    if (ct == 0) {
+      for (int p = 0; p < ar.world; ++p) red_release_sys_add(ar.peer_done[p], 1u);
+      wait_at_least(ar.done, ar.epoch * ar.world * gridDim.x, abort_flag, wd);
+    }
+    comm_bar_sync();
   }
 
   tc_fence_before();
@@ -461,11 +596,12 @@ TcPlan plan_tc(int M, int N, int K, int BN, int sms, bool allow_split) {
   return p;
 }
 
-template <typename T, int BN, int STAGES>
+template <typename T, int BN, int STAGES, bool kFused = false>
 int launch_tc(void* c, const void* a, const void* b, int M, int N, int K, bool bf16,
-              void* workspace, size_t ws_bytes, cudaStream_t stream, const DeviceInfo& info) {
+              void* workspace, size_t ws_bytes, cudaStream_t stream, const DeviceInfo& info,
+              const ArParams* ar = nullptr) {
   using L = TcLayout<BN, STAGES>;
-  auto kernel = gemm_tc_kernel<T, BN, STAGES>;
+  auto kernel = gemm_tc_kernel<T, BN, STAGES, kFused>;
   if (int st = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), L::kAlloc, info)) return st;
   TcPlan p = plan_tc(M, N, K, BN, info.sm_count, workspace != nullptr);
   if (p.ws_bytes > 0 && (ws_bytes < p.ws_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255)))
@@ -482,8 +618,10 @@ int launch_tc(void* c, const void* a, const void* b, int M, int N, int K, bool b
   if (int st = make_tmap_2d_16bit(&tb, b, bf16, K, N, N, 64, kBK)) return st;
   if (int st = make_tmap_2d_16bit(&tc, c, bf16, M, N, N, 64, 32)) return st;
   const uint32_t idesc = idesc_f16(bf16, kBM, BN, /*a_mn_major=*/false, /*b_mn_major=*/true);
-  kernel<<<p.grid, kThreads, L::kAlloc, stream>>>(ta, tb, tc, static_cast<T*>(c), M, N, K, idesc,
-                                                  p.sched);
+  ArParams arp{};
+  if (ar) arp = *ar;
+  kernel<<<p.grid, kFused ? kThreadsFused : kThreads, L::kAlloc, stream>>>(
+      ta, tb, tc, static_cast<T*>(c), M, N, K, idesc, p.sched, arp);
   return check_launch("tcgen05 gemm");
 }
 
@@ -510,6 +648,45 @@ int gemm_tc(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t
     return launch_tc<__nv_bfloat16, kTcBN, kTcStages>(c, a, b, m, n, k, true, workspace, ws_bytes,
                                                       s, info);
   return launch_tc<__half, kTcBN, kTcStages>(c, a, b, m, n, k, false, workspace, ws_bytes, s, info);
+}
+
+int gemm_allreduce_tiles(int64_t M, int64_t N) {
+  return static_cast<int>(((M + kBM - 1) / kBM) * ((N + kTcBN - 1) / kTcBN));
+}
+
+int gemm_allreduce(const void* a, const void* b, int64_t M, int64_t N, int64_t K, int dtype,
+                   const aotk_allreduce_buffers* bufs, void* stream) {
+  DeviceInfo info;
+  if (int st = current_device_info(&info)) return st;
+  if (int st = require_sm100(info)) return st;
+  if (!bufs) return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_gemm_allreduce: null buffers");
+  if (int st = check_tc_preconditions("aotk_gemm_allreduce", bufs->part, a, b, M, N, K, dtype))
+    return st;
+  if (bufs->world < 1 || bufs->rank < 0 || bufs->rank >= bufs->world || bufs->epoch == 0 ||
+      !bufs->part_multicast || !bufs->out_multicast || !bufs->counters || !bufs->peer_counters ||
+      !bufs->done || !bufs->peer_done)
+    return fail(AOTK_ERR_INVALID_ARGUMENT,
+                "aotk_gemm_allreduce: incomplete buffers (rank %d of %d, epoch %u)", bufs->rank,
+                bufs->world, bufs->epoch);
+  if ((bufs->part_multicast & 15u) || (bufs->out_multicast & 15u))
+    return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_gemm_allreduce: multicast addresses not 16-byte aligned");
+  ArParams ar{};
+  ar.rank = bufs->rank;
+  ar.world = bufs->world;
+  ar.part_mc = bufs->part_multicast;
+  ar.out_mc = bufs->out_multicast;
+  ar.counters = bufs->counters;
+  ar.peer_counters = bufs->peer_counters;
+  ar.done = bufs->done;
+  ar.peer_done = bufs->peer_done;
+  ar.epoch = bufs->epoch;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int m = (int)M, n = (int)N, k = (int)K;
+  if (dtype == AOTK_BFLOAT16)
+    return launch_tc<__nv_bfloat16, kTcBN, kTcStages, true>(bufs->part, a, b, m, n, k, true, nullptr,
+                                                            0, s, info, &ar);
+  return launch_tc<__half, kTcBN, kTcStages, true>(bufs->part, a, b, m, n, k, false, nullptr, 0, s,
+                                                   info, &ar);
 }
 
 int tc_watchdog(uint32_t* status, bool clear) {
