@@ -184,7 +184,7 @@ AOTK_API int aotk_gemm_allreduce_tiles(int64_t M, int64_t N, int64_t* tiles);
 /* out = sum over ranks of A_r[M, K] * B_r[K, N], on every rank of a
  * tensor-parallel group (one process per GPU), in one kernel: each rank's
  * persistent tcgen05 GEMM stores its partial tiles into `part`, and as the
- * W partials of a tile arrive, the tile's owner rank (tile % W) sums them
+ * W partials of a tile arrive, the tile's owner rank (one of W, rotating) sums them
  * through the switch (multimem.ld_reduce, fp32 accumulation) and writes the
  * 16-bit result into every rank's output (multimem.st), overlapping the
  * transfer with the rest of the GEMM.  FLOAT16/BFLOAT16, K % 8 == 0,

@@ -131,7 +131,7 @@ __device__ __forceinline__ void st_global_v4(float* p, uint32_t a, uint32_t b, u
 // Fused all-reduce of the output over W ranks (one process per GPU) through
 // NVSwitch multicast memory.  Each rank stores its partial tile into its own
 // `part` buffer, then bumps the tile's arrival counter on the owner rank
-// (tile % W).  The owner's all-reduce warps wait until all W partials of the
+// (tile_owner: rotates over the ranks from round to round).  The owner's all-reduce warps wait until all W partials of the
 // tile have arrived, read their sum through the multicast address of `part`
 // (multimem.ld_reduce, fp32 accumulation) and write it to every rank's `out`
 // through the multicast address of `out` (multimem.st).  Counters only grow:
@@ -160,6 +160,12 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+// Owner rank of a tile: rotates with the round so that every CTA reduces about
+// 1/W of the tiles it computes (tile = cta + round * grid on every rank).
+__device__ __forceinline__ int tile_owner(int tile, int world) {
+  return (tile % gridDim.x + tile / gridDim.x) % world;
+}
+
 __device__ __forceinline__ void comm_bar_sync() {
   asm volatile("bar.sync 2, 128;" ::: "memory");  // warps 6..9 only
 }
@@ -423,7 +429,8 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
         fence_proxy_async_global();
         fence_sys();
         epilogue_bar_sync();
-        if (warp == 2 && lane == 0) red_release_sys_add(ar.peer_counters[w.tile % ar.world] + w.tile, 1u);
+        if (warp == 2 && lane == 0)
+          red_release_sys_add(ar.peer_counters[tile_owner(w.tile, ar.world)] + w.tile, 1u);
       } else {
         if (w.unit >= 0) {
           // All four warps' partial rows are written; count this unit in.
@@ -496,7 +503,7 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
     constexpr int kVecPerRow = BN * 2 / 16;
     WorkItem w;
     for (int i = 0; work_item(sched, i, w); ++i) {
-      if (w.tile % ar.world != ar.rank) continue;
+      if (tile_owner(w.tile, ar.world) != ar.rank) continue;
       if (ct == 0)
         *peer_ok = wait_at_least(ar.counters + w.tile, ar.epoch * ar.world, abort_flag, wd) ? 1 : 0;
       comm_bar_sync();
@@ -505,13 +512,14 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
       if (!ok) break;
       int mb, nb;
       tile_coords(w.tile, tiles_m, tiles_n, mb, nb);
+      constexpr int kInFlight = 8;  // 16-byte reductions per thread in flight
 #pragma unroll 1
-      for (int v0 = ct; v0 < kBM * kVecPerRow; v0 += 4 * 128) {
-        uint4 val[4];
-        uint64_t off[4];
-        bool live[4];
+      for (int v0 = ct; v0 < kBM * kVecPerRow; v0 += kInFlight * 128) {
+        uint4 val[kInFlight];
+        uint64_t off[kInFlight];
+        bool live[kInFlight];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kInFlight; ++u) {
           const int v = v0 + u * 128;
           const int gr = mb * kBM + v / kVecPerRow;
           const int gc = nb * BN + (v % kVecPerRow) * 8;
@@ -525,7 +533,7 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
           }
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
+        for (int u = 0; u < kInFlight; ++u)
           if (live[u]) multimem_st16(ar.out_mc + off[u], val[u]);
       }
     }
