@@ -200,6 +200,13 @@ AOTK_API int aotk_gemm_allreduce(const void* a, const void* b, int64_t M, int64_
  * device.  clear != 0 resets it to 0 after reading. */
 AOTK_API int aotk_watchdog_status(int device, uint32_t* status, int clear);
 
+/* Runs the kernels' bounded waits with nothing to wait for - an mbarrier
+ * phase no one completes, then a flag no one sets - on `stream`.  Each gives
+ * up after about a second and sets watchdog bit 128 and 64 respectively; the
+ * kernel then returns and the context stays usable.  Tests the failure path
+ * without faulting or hanging the GPU.  No reference counterpart. */
+AOTK_API int aotk_watchdog_selftest(void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -38,6 +38,7 @@ SIGNATURES: dict[str, list] = {
     "aotk_gemm_skinny": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
     "aotk_watchdog_status": [_int, ctypes.POINTER(ctypes.c_uint32), _int],
     "aotk_gemm_allreduce_tiles": [_i64, _i64, ctypes.POINTER(ctypes.c_int64)],
+    "aotk_watchdog_selftest": [_ptr],
     "aotk_gemm_allreduce": [_ptr, _ptr, _i64, _i64, _i64, _int, ctypes.c_void_p, _ptr],
 }
 
@@ -184,6 +185,10 @@ def gemm_allreduce_tiles(M: int, N: int) -> int:
 def gemm_allreduce(a, b, M, N, K, dtype, bufs: AllReduceBuffers, stream=None) -> None:
     _call("aotk_gemm_allreduce", _p(a), _p(b), M, N, K, dtype, ctypes.addressof(bufs),
           _stream(stream))
+
+
+def watchdog_selftest(stream=None) -> None:
+    _call("aotk_watchdog_selftest", _stream(stream))
 
 
 def watchdog_status(device: int = 0, clear: bool = True) -> int:

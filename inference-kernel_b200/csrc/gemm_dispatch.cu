@@ -169,3 +169,5 @@ extern "C" int aotk_watchdog_status(int device, uint32_t* status, int clear) {
   cudaSetDevice(prev);
   return st;
 }
+
+extern "C" int aotk_watchdog_selftest(void* stream) { return aotk::watchdog_selftest(stream); }

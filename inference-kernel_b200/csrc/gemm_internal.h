@@ -29,6 +29,9 @@ int gemm_skinny(void* c, const void* a, const void* b, int64_t M, int64_t N, int
 int gemm_simt(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K, int dtype,
               void* stream);
 
+// Launches the bounded-wait self-test kernel (gemm_tc.cu).
+int watchdog_selftest(void* stream);
+
 // Watchdog words of the tensor-core kernels (OR-ed into *status).
 int tc_watchdog(uint32_t* status, bool clear);
 int skinny_watchdog(uint32_t* status, bool clear);

@@ -52,7 +52,9 @@ constexpr int kThreadsFused = 320;  // + 4 all-reduce warps (gemm_allreduce)
 constexpr int kGroupM = 16;  // M tiles per raster group
 constexpr int kMaxSplits = 4;
 
-enum : unsigned { kWdProducer = 1u, kWdMma = 2u, kWdEpilogue = 4u, kWdPeer = 64u };
+enum : unsigned { kWdProducer = 1u, kWdMma = 2u, kWdEpilogue = 4u, kWdPeer = 64u, kWdSelfTest = 128u };
+
+__device__ unsigned g_never_set;  // stays 0: the self-test's flag that nothing sets
 
 template <int BN, int STAGES>
 struct TcLayout {
@@ -556,6 +558,25 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
   }
 }
 
+// Exercises the bounded waits with nothing to wait for: an mbarrier phase that
+// no thread or copy completes, then a flag that nothing sets.  Each gives up
+// after kWaitLimitCycles and records its watchdog bit; the kernel returns.
+__global__ void watchdog_selftest_kernel() {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_addr(&bar), 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_wait_bounded(smem_addr(&bar), 0, &abort_flag, &g_tc_watchdog, kWdSelfTest);
+    abort_flag = 0;
+    wait_at_least(&g_never_set, 1u, &abort_flag, &g_tc_watchdog);
+  }
+}
+
 struct TcPlan {
   int grid;
   TcSched sched;
@@ -695,6 +716,11 @@ int gemm_allreduce(const void* a, const void* b, int64_t M, int64_t N, int64_t K
                                                             0, s, info, &ar);
   return launch_tc<__half, kTcBN, kTcStages, true>(bufs->part, a, b, m, n, k, false, nullptr, 0, s,
                                                    info, &ar);
+}
+
+int watchdog_selftest(void* stream) {
+  watchdog_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>();
+  return check_launch("watchdog self-test");
 }
 
 int tc_watchdog(uint32_t* status, bool clear) {
