@@ -147,6 +147,12 @@ AOTK_API int aotk_gemm(void* c, const void* a, const void* b, int64_t M, int64_t
 AOTK_API int aotk_gemm_tc(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
                  int dtype, void* stream);
 
+/* Persistent tcgen05 kernel on CTA pairs (cta_group::2, 2-CTA clusters),
+ * 256 x 256 tiles: each CTA of a pair stages 128 rows of A and 128 columns of
+ * B, one MMA of M = 256 reads both.  Same preconditions as aotk_gemm_tc. */
+AOTK_API int aotk_gemm_tc2(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
+                           int dtype, void* stream);
+
 /* Skinny (decode) kernel: computes C^T = B^T A^T on tcgen05 with the weight
  * streamed by TMA and K split across a thread-block cluster whose partial sums
  * are reduced through distributed shared memory.  Same preconditions as

@@ -35,6 +35,7 @@ SIGNATURES: dict[str, list] = {
     "aotk_gemm_opt_noalloc": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
     "aotk_gemm": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
     "aotk_gemm_tc": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
+    "aotk_gemm_tc2": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
     "aotk_gemm_skinny": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
     "aotk_watchdog_status": [_int, ctypes.POINTER(ctypes.c_uint32), _int],
     "aotk_gemm_allreduce_tiles": [_i64, _i64, ctypes.POINTER(ctypes.c_int64)],
@@ -170,6 +171,10 @@ def gemm(c, a, b, M, N, K, dtype, stream=None) -> None:
 
 def gemm_tc(c, a, b, M, N, K, dtype, stream=None) -> None:
     _gemm("aotk_gemm_tc", c, a, b, M, N, K, dtype, stream)
+
+
+def gemm_tc2(c, a, b, M, N, K, dtype, stream=None) -> None:
+    _gemm("aotk_gemm_tc2", c, a, b, M, N, K, dtype, stream)
 
 
 def gemm_skinny(c, a, b, M, N, K, dtype, stream=None) -> None:

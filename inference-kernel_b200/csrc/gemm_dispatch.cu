@@ -138,6 +138,11 @@ extern "C" int aotk_gemm_tc(void* c, const void* a, const void* b, int64_t M, in
   return aotk::gemm_tc(c, a, b, M, N, K, dtype, nullptr, 0, stream);
 }
 
+extern "C" int aotk_gemm_tc2(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
+                             int dtype, void* stream) {
+  return aotk::gemm_tc2(c, a, b, M, N, K, dtype, stream);
+}
+
 extern "C" int aotk_gemm_skinny(void* c, const void* a, const void* b, int64_t M, int64_t N,
                                 int64_t K, int dtype, void* stream) {
   return aotk::gemm_skinny(c, a, b, M, N, K, dtype, stream);
@@ -166,6 +171,7 @@ extern "C" int aotk_watchdog_status(int device, uint32_t* status, int clear) {
   *status = 0;
   int st = tc_watchdog(status, clear != 0);
   if (st == AOTK_OK) st = skinny_watchdog(status, clear != 0);
+  if (st == AOTK_OK) st = tc2_watchdog(status, clear != 0);
   cudaSetDevice(prev);
   return st;
 }

@@ -14,6 +14,11 @@ int gemm_tc(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t
             void* workspace, size_t ws_bytes, void* stream);
 size_t gemm_tc_workspace_size(int64_t M, int64_t N, int64_t K, int sm_count);
 
+// Persistent tcgen05 GEMM on CTA pairs, 256 x 256 tiles (gemm_tc2.cu).
+int gemm_tc2(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K, int dtype,
+             void* stream);
+int tc2_watchdog(uint32_t* status, bool clear);
+
 // Persistent tcgen05 GEMM fused with an all-reduce of C over NVSwitch
 // multicast memory (gemm_tc.cu).
 int gemm_allreduce(const void* a, const void* b, int64_t M, int64_t N, int64_t K, int dtype,

@@ -1,0 +1,356 @@
+// Persistent tcgen05 GEMM on CTA pairs: C[M,N] = A[M,K] * B[K,N].
+//
+// A cluster of two CTAs (on two SMs) computes 256 x 256 output tiles with one
+// tcgen05.mma.cta_group::2 per K step (M = 256, N = 256, K = 16):
+//   * CTA r of the pair TMA-loads rows [m0 + 128r, +128) of A and columns
+//     [n0 + 128r, +128) of B into its own shared memory (4-6 stage ring); the
+//     MMA reads both CTAs' halves, so each SM stages half the B traffic of a
+//     128 x 256 tile for twice the math.  No load is multicast.
+//   * The full barrier of a stage lives in the first CTA: its producer
+//     expects the bytes of both CTAs' loads, the second CTA's loads complete
+//     their bytes there.  The first CTA's MMA warp issues all MMAs and its
+//     commits arrive on the empty / accumulator-full barriers of both CTAs.
+//   * Each CTA's four epilogue warps read their 128 accumulator rows from
+//     their own TMEM (two 256-column accumulators, so the epilogue of one tile
+//     overlaps the MMAs of the next), release the accumulator on the first
+//     CTA's barrier and TMA-store 32 x 64 boxes of C.
+// Every wait is bounded (sm100.cuh); both CTAs meet at a cluster barrier
+// before TMEM is freed and before either exits.
+#include <type_traits>
+
+#include "common.h"
+#include "gemm_internal.h"
+#include "sm100.cuh"
+#include "tmap.h"
+#include "vec.cuh"
+
+namespace aotk {
+namespace {
+
+using namespace sm100;
+
+__device__ unsigned g_tc2_watchdog;
+
+constexpr int kBM = 256;      // rows per pair tile (128 per CTA)
+constexpr int kBN = 256;      // columns per pair tile (128 of B per CTA)
+constexpr int kHalf = 128;
+constexpr int kBK = 64;
+constexpr int kUmmaK = 16;
+constexpr int kThreads = 192;
+constexpr int kGroupM = 8;    // M pair-tiles per raster group
+constexpr uint32_t kTmemCols = 2 * kBN;
+
+enum : unsigned { kWdProducer = 256u, kWdMma = 512u, kWdEpilogue = 1024u };
+
+template <int STAGES>
+struct Tc2Layout {
+  static constexpr uint32_t kABytes = kHalf * kBK * 2;  // this CTA's 128 rows of A
+  static constexpr uint32_t kBBox = kBK * 128;          // 64 (N) x 64 (K)
+  static constexpr uint32_t kBBytes = 2 * kBBox;        // this CTA's 128 columns of B
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kPairStageBytes = 2 * kStageBytes;
+  static constexpr uint32_t kCBuf = 32 * 128;
+  static constexpr uint32_t kOffA = 0;
+  static constexpr uint32_t kOffB = kOffA + STAGES * kABytes;
+  static constexpr uint32_t kOffC = kOffB + STAGES * kBBytes;
+  static constexpr uint32_t kOffBar = kOffC + 4 * 2 * kCBuf;
+  static constexpr uint32_t kNumBars = 2 * STAGES + 5;  // full, empty, tfull x2, tempty x2, drain
+  static constexpr uint32_t kOffMisc = kOffBar + kNumBars * 8;
+  static constexpr uint32_t kBytes = kOffMisc + 16;
+  static constexpr uint32_t kAlloc = kBytes + 1024;
+};
+
+__device__ __forceinline__ void pair_tile_coords(int tile, int tiles_m, int tiles_n, int& mb,
+                                                 int& nb) {
+  const int per_group = kGroupM * tiles_n;
+  const int g = tile / per_group;
+  const int first_m = g * kGroupM;
+  const int gm = min(tiles_m - first_m, kGroupM);
+  const int local = tile - g * per_group;
+  mb = first_m + local % gm;
+  nb = local / gm;
+}
+
+template <typename T, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmC, int M, int N, int K, uint32_t idesc) {
+  using L = Tc2Layout<STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_addr(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw);
+  const uint32_t sA = base + L::kOffA;
+  const uint32_t sB = base + L::kOffB;
+  const uint32_t sC = base + L::kOffC;
+  const uint32_t bar0 = base + L::kOffBar;
+  const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
+  unsigned* wd = &g_tc2_watchdog;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0: issues the MMAs
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  const int num_pairs = static_cast<int>(gridDim.x >> 1);
+  const int tiles_m = (M + kBM - 1) / kBM;
+  const int tiles_n = (N + kBN - 1) / kBN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int kblocks = (K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 8);  // 4 epilogue warps in each CTA of the pair
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_addr(tmem_slot), kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // barriers of both CTAs initialised before any cross-CTA use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
+        int mb, nb;
+        pair_tile_coords(tile, tiles_m, tiles_n, mb, nb);
+        const int row0 = mb * kBM + static_cast<int>(rank) * kHalf;
+        const int col0 = nb * kBN + static_cast<int>(rank) * kHalf;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, wd, kWdProducer)) {
+            ok = false;
+            break;
+          }
+          // The stage's bytes are counted on the first CTA's full barrier.
+          const uint32_t fb = map_to_rank(full_bar(stage), 0);
+          if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), L::kPairStageBytes);
+          tma_load_2d_pair(sA + stage * L::kABytes, &tmA, kb * kBK, row0, fb);
+          tma_load_2d_pair(sB + stage * L::kBBytes, &tmB, col0, kb * kBK, fb);
+          tma_load_2d_pair(sB + stage * L::kBBytes + L::kBBox, &tmB, col0 + 64, kb * kBK, fb);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // The first CTA's full barriers see every load of the pair: drain there.
+      if (rank == 0) {
+        int s = stage;
+        uint32_t p = phase;
+        for (int i = 0; i < STAGES && i < issued; ++i) {
+          if (--s < 0) {
+            s = STAGES - 1;
+            p ^= 1u;
+          }
+          mbar_drain(full_bar(s), p);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (first CTA only) ----------------
+    if (lane == 0 && rank == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
+        if (!mbar_wait_bounded(tempty_bar(acc), acc_phase ^ 1u, abort_flag, wd, kWdMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_bounded(full_bar(stage), phase, abort_flag, wd, kWdMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = sA + stage * L::kABytes;
+          const uint32_t b0 = sB + stage * L::kBBytes;
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            const uint64_t ad = sdesc_sw128(a0 + k * kUmmaK * 2, 16, 1024);
+            const uint64_t bd = sdesc_sw128(b0 + k * kUmmaK * 128, L::kBBox, 1024);
+            umma_f16_pair(d_tmem, ad, bd, idesc, kb > 0 || k > 0);
+          }
+          umma_commit_pair(empty_bar(stage), 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(tfull_bar(acc), 0x3);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      umma_commit_pair(drain_bar, 0x3);
+      mbar_drain(drain_bar, 0);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue (warps 2..5, both CTAs) ----------------
+    const int q = warp & 3;
+    const uint32_t cbuf = sC + (warp - 2) * 2 * L::kCBuf;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int nstore = 0;
+    for (int tile = pair; tile < num_tiles; tile += num_pairs) {
+      int mb, nb;
+      pair_tile_coords(tile, tiles_m, tiles_n, mb, nb);
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait_bounded(tfull_bar(acc), acc_phase, abort_flag, wd, kWdEpilogue);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t trow = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                            static_cast<uint32_t>(acc * kBN);
+      const int store_y = mb * kBM + static_cast<int>(rank) * kHalf + q * 32;
+#pragma unroll 1
+      for (int c = 0; c < kBN / 64; ++c) {
+        uint32_t r[64];
+        tmem_ld_32x32b_x32(trow + c * 64, r);
+        tmem_ld_32x32b_x32(trow + c * 64 + 32, r + 32);
+        tmem_wait_ld();
+        if (c == kBN / 64 - 1) {
+          // Accumulator read: release it on the first CTA's barrier.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(map_to_rank(tempty_bar(acc), 0));
+        }
+        const int store_x = nb * kBN + c * 64;
+        if (store_x >= N || store_y >= M) continue;
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          pk[i] = Elem<T>::pack2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+        const uint32_t buf = cbuf + (nstore & 1) * L::kCBuf;
+        if (nstore >= 2 && lane == 0) bulk_wait_read<1>();
+        __syncwarp();
+        const uint32_t row = buf + lane * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          st_shared_v4(row + ((j ^ (lane & 7)) << 4), pk[4 * j], pk[4 * j + 1], pk[4 * j + 2],
+                       pk[4 * j + 3]);
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, buf, store_x, store_y);
+          bulk_commit();
+        }
+        ++nstore;
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+
+  // Neither CTA frees TMEM or exits while its pair may still use its shared
+  // memory (MMA operands, barriers) or its TMEM.
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
+template <typename T, int STAGES>
+int launch_tc2(void* c, const void* a, const void* b, int M, int N, int K, bool bf16,
+               cudaStream_t stream, const DeviceInfo& info) {
+  using L = Tc2Layout<STAGES>;
+  auto kernel = gemm_tc2_kernel<T, STAGES>;
+  if (int st = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), L::kAlloc, info)) return st;
+  CUtensorMap ta, tb, tc;
+  if (int st = make_tmap_2d_16bit(&ta, a, bf16, M, K, K, kBK, kHalf)) return st;
+  if (int st = make_tmap_2d_16bit(&tb, b, bf16, K, N, N, 64, kBK)) return st;
+  if (int st = make_tmap_2d_16bit(&tc, c, bf16, M, N, N, 64, 32)) return st;
+  const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+  const int max_pairs = info.sm_count / 2;
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = L::kAlloc;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const uint32_t idesc = idesc_f16(bf16, kBM, kBN, /*a_mn_major=*/false, /*b_mn_major=*/true);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, M, N, K, idesc);
+  if (e != cudaSuccess)
+    return fail(AOTK_ERR_CUDA, "tcgen05 pair gemm launch: %s", cudaGetErrorString(e));
+  return check_launch("tcgen05 pair gemm");
+}
+
+constexpr int kTc2Stages = 6;
+
+}  // namespace
+
+int gemm_tc2(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K, int dtype,
+             void* stream) {
+  DeviceInfo info;
+  if (int st = current_device_info(&info)) return st;
+  if (int st = require_sm100(info)) return st;
+  if (int st = check_tc_preconditions("aotk_gemm_tc2", c, a, b, M, N, K, dtype)) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int m = (int)M, n = (int)N, k = (int)K;
+  if (dtype == AOTK_BFLOAT16)
+    return launch_tc2<__nv_bfloat16, kTc2Stages>(c, a, b, m, n, k, true, s, info);
+  return launch_tc2<__half, kTc2Stages>(c, a, b, m, n, k, false, s, info);
+}
+
+int tc2_watchdog(uint32_t* status, bool clear) {
+  unsigned v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_tc2_watchdog, sizeof(v));
+  if (e != cudaSuccess) return fail(AOTK_ERR_CUDA, "watchdog read: %s", cudaGetErrorString(e));
+  if (clear) {
+    const unsigned zero = 0;
+    e = cudaMemcpyToSymbol(g_tc2_watchdog, &zero, sizeof(zero));
+    if (e != cudaSuccess) return fail(AOTK_ERR_CUDA, "watchdog clear: %s", cudaGetErrorString(e));
+  }
+  *status |= v;
+  return AOTK_OK;
+}
+
+}  // namespace aotk

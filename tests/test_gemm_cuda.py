@@ -106,6 +106,18 @@ def test_capi_gemm_tc(shape, dt):
     assert capi.watchdog_status() == 0
 
 
+@pytest.mark.parametrize("shape", TC_SHAPES + [(256, 64, 256), (8192, 1024, 2048)], ids=str)
+@pytest.mark.parametrize("dt", ["bfloat16", "float16"])
+def test_capi_gemm_tc2(shape, dt):
+    from aot_kernel import capi
+
+    M, K, N = shape
+    a, b = _inputs(M, K, N, dt, seed=2 * M + N)
+    got = _run_capi(capi.gemm_tc2, a, b, dt)
+    assert_close_for_gemm(got, ops.gemm(a, b, dt), dt)
+    assert capi.watchdog_status() == 0
+
+
 SKINNY = [(1, 64, 256), (1, 4096, 1024), (3, 328, 520), (16, 1024, 2048), (17, 512, 264),
           (64, 2048, 768), (100, 1000, 1032), (128, 4096, 512)]
 
