@@ -92,6 +92,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int kb0 = static_cast<int>(split) * kb_per_split;
   const int kb1 = min(kblocks, kb0 + kb_per_split);  // the host guarantees kb1 > kb0
 
+  // The next kernel may start its own prologue now; this kernel reads global
+  // memory only after pdl_wait_prior() below.
+  pdl_launch_dependents();
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmB);
     tma_prefetch_desc(&tmA);
@@ -117,6 +120,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
+      pdl_wait_prior();  // inputs may come from the previous kernel on the stream
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, wd, kWdProducer)) break;
         const uint32_t fb = full_bar(stage);
@@ -269,13 +273,17 @@ int launch_skinny(void* c, const void* a, const void* b, int M, int N, int K, bo
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = L::kAlloc;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = static_cast<unsigned>(S);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // Programmatic dependent launch: the prologue (barrier init, TMEM
+  // allocation, descriptor prefetch) overlaps the previous kernel's tail.
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   const uint32_t idesc = idesc_f16(bf16, kTileN, MP, /*a_mn_major=*/true, /*b_mn_major=*/false);
   cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tb, ta, static_cast<T*>(c), M, N, K, kbps, idesc);
   if (e != cudaSuccess)

@@ -49,7 +49,7 @@ constexpr int kBK = 64;  // one 128-byte swizzle row of 16-bit elements
 constexpr int kUmmaK = 16;
 constexpr int kThreads = 192;       // plain GEMM: producer, MMA, 4 epilogue warps
 constexpr int kThreadsFused = 320;  // + 4 all-reduce warps (gemm_allreduce)
-constexpr int kGroupM = 16;  // M tiles per raster group
+constexpr int kGroupM = 32;  // M tiles per raster group (A slab 32 x 128 rows stays in L2)
 constexpr int kMaxSplits = 4;
 
 enum : unsigned { kWdProducer = 1u, kWdMma = 2u, kWdEpilogue = 4u, kWdPeer = 64u, kWdSelfTest = 128u };

@@ -300,6 +300,20 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int m, int n, bool a
          (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// ---- programmatic dependent launch ---------------------------------------------
+
+// Lets the next kernel on the stream (launched with programmatic stream
+// serialisation) start its prologue while this one runs.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Waits until the previous kernel on the stream has completed and its memory
+// operations are visible; a no-op when launched without the dependency.
+__device__ __forceinline__ void pdl_wait_prior() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---- cluster / distributed shared memory -------------------------------------
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
