@@ -49,7 +49,7 @@ constexpr int kBK = 64;  // one 128-byte swizzle row of 16-bit elements
 constexpr int kUmmaK = 16;
 constexpr int kThreads = 192;       // plain GEMM: producer, MMA, 4 epilogue warps
 constexpr int kThreadsFused = 320;  // + 4 all-reduce warps (gemm_allreduce)
-constexpr int kGroupM = 32;  // M tiles per raster group (A slab 32 x 128 rows stays in L2)
+constexpr int kGroupM = 16;  // M tiles per raster group
 constexpr int kMaxSplits = 4;
 
 enum : unsigned { kWdProducer = 1u, kWdMma = 2u, kWdEpilogue = 4u, kWdPeer = 64u, kWdSelfTest = 128u };
@@ -356,6 +356,7 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     int nstore = 0;
+    const uint64_t c_policy = l2_policy_evict_first();
     // Packs 64 fp32 values of this lane's row into 16-bit, stages them in a
     // 128-byte-swizzled 32 x 64 box and TMA-stores the box at (x, y).
     auto store_chunk = [&](const float (&f)[64], int x, int y) {
@@ -375,7 +376,9 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
       fence_proxy_async_shared();
       __syncwarp();
       if (lane == 0) {
-        tma_store_2d(&tmC, buf, x, y);
+        // C is written once and not re-read here: evict it first so the A
+        // and B tiles other CTAs still need stay in L2.
+        tma_store_2d_hint(&tmC, buf, x, y, c_policy);
         bulk_commit();
       }
       ++nstore;
