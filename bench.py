@@ -58,6 +58,7 @@ CASES = {
     "gemm_decode_m16": ("gemm", (16, 4096, 28672)),
     "gemm_m128_down": ("gemm", (128, 14336, 4096)),
     "rms_norm": ("rms_norm", (8192, 4096)),
+    "add_rms_norm": ("add_rms_norm", (8192, 4096)),
     "silu": ("silu", (8192, 14336)),
     "silu_mul": ("silu_mul", (8192, 14336)),
 }
@@ -368,7 +369,11 @@ def kernel_table(peaks: dict) -> dict:
     xs = [rand_bf16((rows, cols), 20 + 2 * i) for i in range(R)]
     out["rms_norm_8192x4096"] = hbm_entry([lambda x=x: aot_kernel.rms_norm(x, w) for x in xs],
                                           2.0 * rows * cols * 2 + cols * 2, R)
-    del xs
+    rs = [rand_bf16((rows, cols), 40 + 2 * i) for i in range(R)]
+    out["add_rms_norm_8192x4096"] = hbm_entry(
+        [lambda x=x, r=r: aot_kernel.add_rmsnorm(x, r, w) for x, r in zip(xs, rs)],
+        4.0 * rows * cols * 2 + cols * 2, R)
+    del xs, rs
     rows, cols = 8192, 14336
     g = rand_bf16((rows, cols), 22, std=2.0)
     u = rand_bf16((rows, cols), 23, std=2.0)
@@ -577,6 +582,11 @@ def run_case(args) -> None:
         x = rand_bf16(shape, 3)
         w = rand_bf16((shape[1],), 4, std=0.1, mean=1.0)
         fn = lambda: aot_kernel.rms_norm(x, w)  # noqa: E731
+    elif kind == "add_rms_norm":
+        x = rand_bf16(shape, 3)
+        r = rand_bf16(shape, 8)
+        w = rand_bf16((shape[1],), 4, std=0.1, mean=1.0)
+        fn = lambda: aot_kernel.add_rmsnorm(x, r, w)  # noqa: E731
     elif kind == "silu":
         x = rand_bf16(shape, 5, std=2.0)
         fn = lambda: aot_kernel.silu(x)  # noqa: E731

@@ -88,6 +88,15 @@ AOTK_API int aotk_silu_mul_forward(void* out, int64_t out_stride, const void* ga
 AOTK_API int aotk_rmsnorm_forward(void* out, const void* x, const void* weight, int64_t rows,
                          int64_t cols, double eps, int dtype, void* stream);
 
+/* h = x + residual rounded to `dtype`, written to residual_out, and
+ * out = rmsnorm(h, weight, eps) as aotk_rmsnorm_forward computes it - one pass
+ * over x and residual.  What the reference computes as ref.rmsnorm(x + r, w)
+ * with the addition a separate 16-bit op (ref/norm.py:11-12); no fused
+ * counterpart in the reference.  residual_out may alias residual. */
+AOTK_API int aotk_add_rmsnorm_forward(void* out, void* residual_out, const void* x,
+                                      const void* residual, const void* weight, int64_t rows,
+                                      int64_t cols, double eps, int dtype, void* stream);
+
 /* ---- gemm ------------------------------------------------------------- */
 
 /* Tensor-core GEMM for FLOAT16 / BFLOAT16 (FLOAT32 returns AOTK_ERR_UNSUPPORTED,

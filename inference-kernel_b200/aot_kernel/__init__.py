@@ -5,16 +5,17 @@ Importing the package loads ``_C`` (the torch operator library, built in place
 by ``inference-kernel_b200/build.py``), which registers ``torch.ops.aot_kernel.*``
 and pulls in ``libaotk.so`` (the CUDA kernels and their C ABI).  Names and
 signatures follow the reference's ``aot_kernel/__init__.py:8-20``; ``rms_norm``
-is an alias of ``rmsnorm`` and ``silu_mul`` is new.
+is an alias of ``rmsnorm``; ``silu_mul`` and ``add_rmsnorm`` are new fused ops.
 """
 
 from .activation import relu, silu, silu_mul
 from .gemm import gemm, gemm_naive
-from .norm import rms_norm, rmsnorm
+from .norm import add_rmsnorm, rms_norm, rmsnorm
 
 __version__ = "0.1.0"
 
 __all__ = [
+    "add_rmsnorm",
     "gemm",
     "gemm_naive",
     "relu",

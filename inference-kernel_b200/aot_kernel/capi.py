@@ -29,6 +29,8 @@ SIGNATURES: dict[str, list] = {
     "aotk_relu_forward": [_ptr, _ptr, _i64, _int, _ptr],
     "aotk_silu_mul_forward": [_ptr, _i64, _ptr, _i64, _ptr, _i64, _i64, _i64, _int, _ptr],
     "aotk_rmsnorm_forward": [_ptr, _ptr, _ptr, _i64, _i64, ctypes.c_double, _int, _ptr],
+    "aotk_add_rmsnorm_forward": [_ptr, _ptr, _ptr, _ptr, _ptr, _i64, _i64, ctypes.c_double, _int,
+                                 _ptr],
     "aotk_gemm_opt": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
     "aotk_gemm_opt_ws": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr, ctypes.c_size_t, _ptr],
     "aotk_gemm_opt_workspace_size": [_i64, _i64, _i64, _int, ctypes.POINTER(ctypes.c_size_t)],
@@ -139,6 +141,12 @@ def rmsnorm_forward(out, x, weight, rows: int, cols: int, eps: float, dtype: int
                     stream=None) -> None:
     _call("aotk_rmsnorm_forward", _p(out), _p(x), _p(weight), rows, cols, eps, dtype,
           _stream(stream))
+
+
+def add_rmsnorm_forward(out, residual_out, x, residual, weight, rows: int, cols: int, eps: float,
+                        dtype: int, stream=None) -> None:
+    _call("aotk_add_rmsnorm_forward", _p(out), _p(residual_out), _p(x), _p(residual), _p(weight),
+          rows, cols, eps, dtype, _stream(stream))
 
 
 def _gemm(name, c, a, b, M, N, K, dtype, stream) -> None:

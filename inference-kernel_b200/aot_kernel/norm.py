@@ -19,3 +19,23 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.T
 
 
 rms_norm = rmsnorm
+
+
+def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                eps: float = 1e-6) -> tuple[torch.Tensor, torch.Tensor]:
+    """(rmsnorm(h, weight, eps), h) with h = x + residual rounded to the dtype.
+
+    The pre-norm step of a transformer block in one pass: equal to
+    ``rmsnorm(x + residual, weight, eps)`` and ``x + residual``.
+    """
+    if not x.is_cuda:
+        raise ValueError("cuda add_rmsnorm requires a CUDA tensor")
+    assert_contiguous(x, residual, weight)
+    assert_same_device(x, residual, weight)
+    assert_same_dtype(x, residual, weight)
+    if x.shape != residual.shape:
+        raise ValueError(f"shape mismatch: x {tuple(x.shape)} vs residual {tuple(residual.shape)}")
+    out = torch.empty_like(x)
+    h = torch.empty_like(x)
+    torch.ops.aot_kernel.add_rmsnorm_forward(out, h, x, residual, weight, eps)
+    return out, h

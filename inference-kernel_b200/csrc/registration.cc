@@ -125,6 +125,32 @@ void rmsnorm_forward(at::Tensor out, at::Tensor x, at::Tensor weight, double eps
                op);
 }
 
+void add_rmsnorm_forward(at::Tensor out, at::Tensor residual_out, at::Tensor x,
+                         at::Tensor residual, at::Tensor weight, double eps) {
+  const char* op = "add_rmsnorm";
+  check_cuda(x, op, "x");
+  check_cuda(residual, op, "residual");
+  check_cuda(weight, op, "weight");
+  check_same(x, residual, op, "x", "residual");
+  check_same(x, weight, op, "x", "weight");
+  TORCH_CHECK(x.is_contiguous() && residual.is_contiguous() && weight.is_contiguous(), "[", op,
+              "] inputs must be contiguous");
+  TORCH_CHECK(x.sizes() == residual.sizes(), "[", op, "] x and residual shapes differ: ", x.sizes(),
+              " vs ", residual.sizes());
+  TORCH_CHECK(weight.dim() == 1 && x.dim() >= 1 && weight.size(0) == x.size(-1), "[", op,
+              "] weight must be [x.size(-1)]");
+  check_out_like(out, x, op);
+  check_out_like(residual_out, x, op);
+  if (x.numel() == 0) return;
+  const int64_t cols = x.size(-1);
+  const int64_t rows = x.numel() / cols;
+  c10::cuda::CUDAGuard guard(x.device());
+  check_status(aotk_add_rmsnorm_forward(out.data_ptr(), residual_out.data_ptr(), x.data_ptr(),
+                                        residual.data_ptr(), weight.data_ptr(), rows, cols, eps,
+                                        aotk_dtype(x, op), current_stream(x)),
+               op);
+}
+
 struct GemmArgs {
   int64_t M, N, K;
   int dtype;
@@ -188,6 +214,11 @@ TORCH_LIBRARY(aot_kernel, m) {
 
   m.def("rmsnorm_forward(Tensor! out, Tensor x, Tensor weight, float eps) -> ()");
   m.impl("rmsnorm_forward", c10::kCUDA, &rmsnorm_forward);
+
+  m.def(
+      "add_rmsnorm_forward(Tensor! out, Tensor! residual_out, Tensor x, Tensor residual, Tensor "
+      "weight, float eps) -> ()");
+  m.impl("add_rmsnorm_forward", c10::kCUDA, &add_rmsnorm_forward);
 
   m.def("gemm(Tensor! out, Tensor a, Tensor b) -> ()");
   m.impl("gemm", c10::kCUDA, &gemm);

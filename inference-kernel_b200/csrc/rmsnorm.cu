@@ -9,6 +9,12 @@
 // reduction and reads x twice (aot_kernel/csrc/norm/rmsnorm.cu:111-182).
 // Rows whose byte length is not a multiple of 16 take a scalar two-pass
 // kernel, as the reference does (rmsnorm.cu:205-209).
+//
+// The residual variant (aotk_add_rmsnorm_forward) first forms h = x + residual
+// rounded to the element type - what `rmsnorm(x + residual)` sees when the
+// addition is a separate 16-bit op - writes h out as the next residual and
+// normalises h, all in the same pass: x and residual are read once, h and y
+// written once.
 #include "common.h"
 #include "vec.cuh"
 
@@ -35,10 +41,13 @@ __device__ __forceinline__ void load_row(const T* __restrict__ x, int64_t row, i
 // Persistent over row groups: a block owns RPB rows at a time and, before
 // reducing them, issues the loads of the group it will handle next, so each
 // SM keeps two groups of rows in flight and the grid is a single wave.
-template <typename T, int VPT, int TPR>
+// With kRes, the loaded vectors are x and residual and the row is their
+// rounded sum h, which is also written to h_out.
+template <typename T, int VPT, int TPR, bool kRes>
 __global__ void __launch_bounds__(TPR > kBlock ? TPR : kBlock)
-    rmsnorm_vec_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y,
-                       int64_t rows, int cols, float eps) {
+    rmsnorm_vec_kernel(const T* __restrict__ x, const T* __restrict__ res, const T* __restrict__ w,
+                       T* __restrict__ y, T* __restrict__ h_out, int64_t rows, int cols,
+                       float eps) {
   constexpr int E = Elem<T>::kPerVec;
   constexpr int THREADS = TPR > kBlock ? TPR : kBlock;
   constexpr int RPB = THREADS / TPR;  // rows per block
@@ -53,12 +62,32 @@ __global__ void __launch_bounds__(TPR > kBlock ? TPR : kBlock)
   const int64_t groups = (rows + RPB - 1) / RPB;
   const uint4* wr = reinterpret_cast<const uint4*>(w);
 
-  uint4 cur[VPT];
+  uint4 cur[VPT], cur_r[kRes ? VPT : 1];
   int64_t g = blockIdx.x;
   load_row<T, VPT, TPR>(x, g * RPB + sub, rows, cols, t, cur);
+  if constexpr (kRes) load_row<T, VPT, TPR>(res, g * RPB + sub, rows, cols, t, cur_r);
   for (int iter = 0; g < groups; g += gridDim.x, ++iter) {
-    uint4 nxt[VPT];
-    if constexpr (kPrefetch) load_row<T, VPT, TPR>(x, (g + gridDim.x) * RPB + sub, rows, cols, t, nxt);
+    uint4 nxt[VPT], nxt_r[kRes ? VPT : 1];
+    if constexpr (kPrefetch) {
+      load_row<T, VPT, TPR>(x, (g + gridDim.x) * RPB + sub, rows, cols, t, nxt);
+      if constexpr (kRes) load_row<T, VPT, TPR>(res, (g + gridDim.x) * RPB + sub, rows, cols, t, nxt_r);
+    }
+    const int64_t row = g * RPB + sub;
+    if constexpr (kRes) {
+      // h = round(x + residual); the normalisation below sees exactly h.
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        float a[E], b[E];
+        Elem<T>::unpack(cur[i], a);
+        Elem<T>::unpack(cur_r[i], b);
+#pragma unroll
+        for (int e = 0; e < E; ++e) a[e] += b[e];
+        cur[i] = Elem<T>::pack(a);
+        const int idx = t + i * TPR;
+        if (row < rows && idx < n_vec)
+          st_stream(reinterpret_cast<uint4*>(h_out + row * (int64_t)cols) + idx, cur[i]);
+      }
+    }
 
     float ss = 0.0f;
 #pragma unroll
@@ -79,7 +108,6 @@ __global__ void __launch_bounds__(TPR > kBlock ? TPR : kBlock)
       for (int k = 0; k < WPR; ++k) ss += partial[iter & 1][sub][k];
     }
     const float rstd = rsqrtf(ss / (float)cols + eps);
-    const int64_t row = g * RPB + sub;
     if (row < rows) {
       uint4* yr = reinterpret_cast<uint4*>(y + row * (int64_t)cols);
 #pragma unroll
@@ -97,25 +125,37 @@ __global__ void __launch_bounds__(TPR > kBlock ? TPR : kBlock)
     }
     if constexpr (kPrefetch) {
 #pragma unroll
-      for (int i = 0; i < VPT; ++i) cur[i] = nxt[i];
+      for (int i = 0; i < VPT; ++i) {
+        cur[i] = nxt[i];
+        if constexpr (kRes) cur_r[i] = nxt_r[i];
+      }
     } else {
       load_row<T, VPT, TPR>(x, (g + gridDim.x) * RPB + sub, rows, cols, t, cur);
+      if constexpr (kRes) load_row<T, VPT, TPR>(res, (g + gridDim.x) * RPB + sub, rows, cols, t, cur_r);
     }
   }
 }
 
-// Any row length: one block per row, two passes over x (the second mostly hits L2).
-template <typename T>
+// Any row length: one block per row, two passes over the row (the second
+// mostly hits L2).  With a residual, pass one also writes h = round(x + r) and
+// pass two reads h back.
+template <typename T, bool kRes>
 __global__ void __launch_bounds__(kBlock) rmsnorm_scalar_kernel(const T* __restrict__ x,
+                                                                const T* __restrict__ res,
                                                                 const T* __restrict__ w,
-                                                                T* __restrict__ y, int64_t cols,
-                                                                float eps) {
+                                                                T* __restrict__ y,
+                                                                T* __restrict__ h_out,
+                                                                int64_t cols, float eps) {
   __shared__ float partial[kBlock / 32];
-  const T* xr = x + (int64_t)blockIdx.x * cols;
-  T* yr = y + (int64_t)blockIdx.x * cols;
+  const int64_t off = (int64_t)blockIdx.x * cols;
   float ss = 0.0f;
   for (int64_t c = threadIdx.x; c < cols; c += kBlock) {
-    const float f = Elem<T>::to_f(xr[c]);
+    float f = Elem<T>::to_f(x[off + c]);
+    if constexpr (kRes) {
+      const T h = Elem<T>::from_f(f + Elem<T>::to_f(res[off + c]));
+      h_out[off + c] = h;
+      f = Elem<T>::to_f(h);
+    }
     ss = fmaf(f, f, ss);
   }
 #pragma unroll
@@ -126,18 +166,20 @@ __global__ void __launch_bounds__(kBlock) rmsnorm_scalar_kernel(const T* __restr
 #pragma unroll
   for (int k = 0; k < kBlock / 32; ++k) ss += partial[k];
   const float rstd = rsqrtf(ss / (float)cols + eps);
+  const T* src = kRes ? h_out : x;  // each thread re-reads only what it wrote
   for (int64_t c = threadIdx.x; c < cols; c += kBlock) {
-    yr[c] = Elem<T>::from_f(Elem<T>::to_f(xr[c]) * rstd * Elem<T>::to_f(w[c]));
+    y[off + c] = Elem<T>::from_f(Elem<T>::to_f(src[off + c]) * rstd * Elem<T>::to_f(w[c]));
   }
 }
 
-template <typename T, int VPT, int TPR>
-int launch_vec(const T* x, const T* w, T* y, int64_t rows, int cols, float eps, cudaStream_t s) {
+template <typename T, int VPT, int TPR, bool kRes>
+int launch_vec(const T* x, const T* r, const T* w, T* y, T* h, int64_t rows, int cols, float eps,
+               cudaStream_t s) {
   constexpr int THREADS = TPR > kBlock ? TPR : kBlock;
   constexpr int RPB = THREADS / TPR;
   DeviceInfo info;
   if (int st = current_device_info(&info)) return st;
-  auto kernel = rmsnorm_vec_kernel<T, VPT, TPR>;
+  auto kernel = rmsnorm_vec_kernel<T, VPT, TPR, kRes>;
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, THREADS, 0) != cudaSuccess ||
       per_sm < 1)
@@ -145,37 +187,62 @@ int launch_vec(const T* x, const T* w, T* y, int64_t rows, int cols, float eps, 
   const int64_t groups = (rows + RPB - 1) / RPB;
   const int64_t capacity = (int64_t)per_sm * info.sm_count;
   const int64_t blocks = groups < capacity ? groups : capacity;
-  kernel<<<(unsigned)blocks, THREADS, 0, s>>>(x, w, y, rows, cols, eps);
+  kernel<<<(unsigned)blocks, THREADS, 0, s>>>(x, r, w, y, h, rows, cols, eps);
   return check_launch("aotk_rmsnorm_forward");
 }
 
-template <typename T>
-int launch(const void* xv, const void* wv, void* yv, int64_t rows, int64_t cols, float eps,
-           cudaStream_t s) {
+template <typename T, bool kRes>
+int launch(const void* xv, const void* rv, const void* wv, void* yv, void* hv, int64_t rows,
+           int64_t cols, float eps, cudaStream_t s) {
   const T* x = static_cast<const T*>(xv);
+  const T* r = static_cast<const T*>(rv);
   const T* w = static_cast<const T*>(wv);
   T* y = static_cast<T*>(yv);
+  T* h = static_cast<T*>(hv);
   constexpr int E = Elem<T>::kPerVec;
-  const bool vec_ok = cols % E == 0 && aligned16(x) && aligned16(w) && aligned16(y);
+  const bool vec_ok = cols % E == 0 && aligned16(x) && aligned16(w) && aligned16(y) &&
+                      (!kRes || (aligned16(r) && aligned16(h)));
   const int64_t n_vec = cols / E;
-  if (vec_ok && n_vec <= 8 * 1024) {
+  // The residual variant keeps two copies (x, r) of the row per thread: at
+  // most 4 vectors per thread, twice the threads per row.
+  constexpr int kMaxVpt = kRes ? 4 : 8;
+  if (vec_ok && n_vec <= kMaxVpt * 1024) {
     const int nv = (int)n_vec;
     const int c = (int)cols;
-    // Short rows: one warp per row with 1..8 vectors per lane.
-    if (nv <= 32) return launch_vec<T, 1, 32>(x, w, y, rows, c, eps, s);
-    if (nv <= 64) return launch_vec<T, 2, 32>(x, w, y, rows, c, eps, s);
-    if (nv <= 128) return launch_vec<T, 4, 32>(x, w, y, rows, c, eps, s);
-    if (nv <= 256) return launch_vec<T, 8, 32>(x, w, y, rows, c, eps, s);
-    // Long rows: 8 vectors per thread, 64..1024 threads per row.
-    if (nv <= 512) return launch_vec<T, 8, 64>(x, w, y, rows, c, eps, s);
-    if (nv <= 1024) return launch_vec<T, 8, 128>(x, w, y, rows, c, eps, s);
-    if (nv <= 2048) return launch_vec<T, 8, 256>(x, w, y, rows, c, eps, s);
-    if (nv <= 4096) return launch_vec<T, 8, 512>(x, w, y, rows, c, eps, s);
-    return launch_vec<T, 8, 1024>(x, w, y, rows, c, eps, s);
+    // Short rows: one warp per row with 1..kMaxVpt vectors per lane.
+    if (nv <= 32) return launch_vec<T, 1, 32, kRes>(x, r, w, y, h, rows, c, eps, s);
+    if (nv <= 64) return launch_vec<T, 2, 32, kRes>(x, r, w, y, h, rows, c, eps, s);
+    if (nv <= 128) return launch_vec<T, 4, 32, kRes>(x, r, w, y, h, rows, c, eps, s);
+    constexpr int V = kMaxVpt;
+    if (nv <= V * 32) return launch_vec<T, V, 32, kRes>(x, r, w, y, h, rows, c, eps, s);
+    // Long rows: kMaxVpt vectors per thread, 64..1024 threads per row.
+    if (nv <= V * 64) return launch_vec<T, V, 64, kRes>(x, r, w, y, h, rows, c, eps, s);
+    if (nv <= V * 128) return launch_vec<T, V, 128, kRes>(x, r, w, y, h, rows, c, eps, s);
+    if (nv <= V * 256) return launch_vec<T, V, 256, kRes>(x, r, w, y, h, rows, c, eps, s);
+    if (nv <= V * 512) return launch_vec<T, V, 512, kRes>(x, r, w, y, h, rows, c, eps, s);
+    return launch_vec<T, V, 1024, kRes>(x, r, w, y, h, rows, c, eps, s);
   }
   if (rows > 0x7fffffffLL) return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_rmsnorm_forward: too many rows");
-  rmsnorm_scalar_kernel<T><<<(unsigned)rows, kBlock, 0, s>>>(x, w, y, cols, eps);
+  rmsnorm_scalar_kernel<T, kRes><<<(unsigned)rows, kBlock, 0, s>>>(x, r, w, y, h, cols, eps);
   return check_launch("aotk_rmsnorm_forward");
+}
+
+template <bool kRes>
+int dispatch(const void* x, const void* r, const void* w, void* y, void* h, int64_t rows,
+             int64_t cols, double eps, int dtype, void* stream, const char* name) {
+  if (rows < 0 || cols < 0) return fail(AOTK_ERR_INVALID_ARGUMENT, "%s: negative size", name);
+  if (rows == 0 || cols == 0) return AOTK_OK;
+  if (!y || !x || !w || (kRes && (!r || !h)))
+    return fail(AOTK_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
+  if (cols > 0x7fffffffLL) return fail(AOTK_ERR_INVALID_ARGUMENT, "%s: row too long", name);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const float e = static_cast<float>(eps);
+  switch (dtype) {
+    case AOTK_FLOAT32: return launch<float, kRes>(x, r, w, y, h, rows, cols, e, s);
+    case AOTK_FLOAT16: return launch<__half, kRes>(x, r, w, y, h, rows, cols, e, s);
+    case AOTK_BFLOAT16: return launch<__nv_bfloat16, kRes>(x, r, w, y, h, rows, cols, e, s);
+    default: return fail(AOTK_ERR_UNSUPPORTED, "%s: unsupported dtype %d", name, dtype);
+  }
 }
 
 }  // namespace
@@ -183,17 +250,13 @@ int launch(const void* xv, const void* wv, void* yv, int64_t rows, int64_t cols,
 
 extern "C" int aotk_rmsnorm_forward(void* out, const void* x, const void* weight, int64_t rows,
                                     int64_t cols, double eps, int dtype, void* stream) {
-  using namespace aotk;
-  if (rows < 0 || cols < 0) return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_rmsnorm_forward: negative size");
-  if (rows == 0 || cols == 0) return AOTK_OK;
-  if (!out || !x || !weight) return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_rmsnorm_forward: null pointer");
-  if (cols > 0x7fffffffLL) return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_rmsnorm_forward: row too long");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const float e = static_cast<float>(eps);
-  switch (dtype) {
-    case AOTK_FLOAT32: return launch<float>(x, weight, out, rows, cols, e, s);
-    case AOTK_FLOAT16: return launch<__half>(x, weight, out, rows, cols, e, s);
-    case AOTK_BFLOAT16: return launch<__nv_bfloat16>(x, weight, out, rows, cols, e, s);
-    default: return fail(AOTK_ERR_UNSUPPORTED, "aotk_rmsnorm_forward: unsupported dtype %d", dtype);
-  }
+  return aotk::dispatch<false>(x, nullptr, weight, out, nullptr, rows, cols, eps, dtype, stream,
+                               "aotk_rmsnorm_forward");
+}
+
+extern "C" int aotk_add_rmsnorm_forward(void* out, void* residual_out, const void* x,
+                                        const void* residual, const void* weight, int64_t rows,
+                                        int64_t cols, double eps, int dtype, void* stream) {
+  return aotk::dispatch<true>(x, residual, weight, out, residual_out, rows, cols, eps, dtype,
+                              stream, "aotk_add_rmsnorm_forward");
 }

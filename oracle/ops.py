@@ -75,6 +75,14 @@ def rmsnorm(x: np.ndarray, weight: np.ndarray, eps: float, dtype: str) -> np.nda
     return round_to((x * rstd) * w, dtype)
 
 
+def add_rmsnorm(x: np.ndarray, residual: np.ndarray, weight: np.ndarray, eps: float, dtype: str):
+    """(``ref.rmsnorm(x + r, w, eps)``, ``x + r``): the 16-bit addition rounds
+    (torch's elementwise add of two 16-bit tensors computes in fp32 and rounds
+    once), then rmsnorm of the rounded sum."""
+    h = round_to(np.asarray(x, dtype=np.float32) + np.asarray(residual, dtype=np.float32), dtype)
+    return rmsnorm(h, weight, eps, dtype), h
+
+
 def _silu_f32(x: np.ndarray) -> np.ndarray:
     x = np.asarray(x, dtype=np.float32)
     with np.errstate(over="ignore"):

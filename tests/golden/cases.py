@@ -21,7 +21,7 @@ def seed_of(case_id: str) -> int:
 
 @dataclass(frozen=True)
 class Case:
-    op: str                     # gemm | rmsnorm | silu | relu | silu_mul
+    op: str                     # gemm | rmsnorm | add_rmsnorm | silu | relu | silu_mul
     shape: tuple                # gemm: (M, K, N); others: input shape
     dtype: str
     eps: float = 1e-6
@@ -45,6 +45,7 @@ GEMM_SHAPES = [(8, 16, 8), (32, 64, 32), (17, 33, 23), (64, 128, 32), (128, 256,
 RMSNORM_SHAPES = [(8, 16), (32, 64), (4, 16, 128), (2, 3, 1023), (8, 8, 8, 16384)]
 ACT_SHAPES = [(1024,), (32, 1024), (4, 16, 1024), (1023,)]
 SILU_MUL_SHAPES = [(4, 1024), (3, 1000), (2, 14336)]
+ADD_RMSNORM_SHAPES = [(4, 4096), (3, 1000), (2, 3, 1023)]
 
 
 def all_cases() -> list[Case]:
@@ -56,6 +57,7 @@ def all_cases() -> list[Case]:
         cases += [Case("silu", s, dt) for s in ACT_SHAPES]
         cases += [Case("relu", s, dt) for s in ACT_SHAPES]
         cases += [Case("silu_mul", s, dt, x_std=2.0) for s in SILU_MUL_SHAPES]
+        cases += [Case("add_rmsnorm", s, dt, w_mean=1.0, w_std=0.1) for s in ADD_RMSNORM_SHAPES]
     # custom eps (tests/norm/test_cuda.py:37-46)
     cases.append(Case("rmsnorm", (4, 32), "float32", eps=1e-3))
     # the CPU-runnable configuration: ref.gemm 1024^3 bf16, N(0,1)
@@ -78,6 +80,10 @@ def make_inputs(case: Case):
         x = randn(case.shape, s, case.dtype, std=case.x_std)
         w = randn((case.shape[-1],), s + 1, case.dtype, mean=case.w_mean, std=case.w_std)
         return (x, w)
+    if case.op == "add_rmsnorm":
+        return (randn(case.shape, s, case.dtype, std=case.x_std),
+                randn(case.shape, s + 2, case.dtype, std=case.x_std),
+                randn((case.shape[-1],), s + 1, case.dtype, mean=case.w_mean, std=case.w_std))
     if case.op in ("silu", "relu"):
         return (randn(case.shape, s, case.dtype, std=case.x_std),)
     if case.op == "silu_mul":
@@ -93,6 +99,8 @@ def oracle_output(case: Case, inputs):
         return ops.gemm(*inputs, case.dtype)
     if case.op == "rmsnorm":
         return ops.rmsnorm(*inputs, case.eps, case.dtype)
+    if case.op == "add_rmsnorm":
+        return ops.add_rmsnorm(*inputs, case.eps, case.dtype)[0]
     if case.op == "silu":
         return ops.silu(*inputs, case.dtype)
     if case.op == "relu":

@@ -50,6 +50,8 @@ def run_reference(ref, case, inputs):
         y = ref.gemm(*t)
     elif case.op == "rmsnorm":
         y = ref.rmsnorm(t[0], t[1], eps=case.eps)
+    elif case.op == "add_rmsnorm":
+        y = ref.rmsnorm(t[0] + t[1], t[2], eps=case.eps)  # the reference composition
     elif case.op == "silu":
         y = ref.silu(t[0])
     elif case.op == "relu":

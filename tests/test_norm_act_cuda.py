@@ -111,7 +111,8 @@ def test_silu_mul_strided_halves(dtype):
 
 # ---- C ABI against the reference's golden outputs ----
 
-GOLDEN_CASES = [c for c in all_cases() if c.op in ("rmsnorm", "silu", "relu", "silu_mul")]
+GOLDEN_CASES = [c for c in all_cases()
+                if c.op in ("rmsnorm", "add_rmsnorm", "silu", "relu", "silu_mul")]
 
 
 @pytest.mark.parametrize("case", GOLDEN_CASES, ids=lambda c: c.id)
@@ -129,6 +130,11 @@ def test_capi_against_reference_golden(case):
     if case.op == "rmsnorm":
         cols = case.shape[-1]
         capi.rmsnorm_forward(out, ins[0], ins[1], ins[0].numel() // cols, cols, case.eps, code)
+    elif case.op == "add_rmsnorm":
+        cols = case.shape[-1]
+        h = torch.empty_like(ins[0])
+        capi.add_rmsnorm_forward(out, h, ins[0], ins[1], ins[2], ins[0].numel() // cols, cols,
+                                 case.eps, code)
     elif case.op in ("silu", "relu"):
         getattr(capi, f"{case.op}_forward")(out, ins[0], ins[0].numel(), code)
     else:
@@ -140,6 +146,38 @@ def test_capi_against_reference_golden(case):
     assert_close_common(got, ref, dt)
     if dt != "float32":
         assert_max_err_frac(got, ref, 1e-2)
+
+
+@pytest.mark.parametrize("shape", [(8, 16), (4, 16, 128), (2, 3, 1023), (33, 4096), (5, 8192),
+                                   (3, 16384), (2, 40000)], ids=str)
+def test_add_rmsnorm_matches_oracle(shape, dtype):
+    from aot_kernel import add_rmsnorm
+
+    x = randn(shape, 31, dtype)
+    r = randn(shape, 32, dtype)
+    w = randn((shape[-1],), 33, dtype, mean=1.0, std=0.1)
+    y, h = add_rmsnorm(to_device(x, dtype), to_device(r, dtype), to_device(w, dtype))
+    ey, eh = ops.add_rmsnorm(x, r, w, 1e-6, dtype)
+    assert_close_np(h, eh, rtol=0, atol=0) if dtype != "float32" else assert_close_common(h, eh, dtype)
+    assert_close_common(y, ey, dtype)
+
+
+def test_add_rmsnorm_in_place_residual():
+    """residual_out may alias residual (the usual in-place update)."""
+    import torch
+
+    from aot_kernel import capi
+
+    x = randn((64, 4096), 34, "bfloat16")
+    r = randn((64, 4096), 35, "bfloat16")
+    w = randn((4096,), 36, "bfloat16", mean=1.0, std=0.1)
+    tx, tr, tw = to_device(x, "bfloat16"), to_device(r, "bfloat16"), to_device(w, "bfloat16")
+    y = torch.empty_like(tx)
+    capi.add_rmsnorm_forward(y, tr, tx, tr, tw, 64, 4096, 1e-6, capi.BFLOAT16)
+    torch.cuda.synchronize()
+    ey, eh = ops.add_rmsnorm(x, r, w, 1e-6, "bfloat16")
+    assert_close_np(tr, eh, rtol=0, atol=0)
+    assert_close_common(y, ey, "bfloat16")
 
 
 # ---- full-size configurations ----
