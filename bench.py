@@ -76,6 +76,8 @@ def parse_args():
     ap.add_argument("--tp-chunks", type=int, default=1)
     ap.add_argument("--tp-allreduce", choices=["nccl", "fused"], default="fused",
                     help="down projection + all-reduce: NCCL after the GEMM, or one fused kernel")
+    ap.add_argument("--tp-unfused-silu", action="store_true",
+                    help="gate/up GEMM then silu_mul, instead of the fused gate/up + silu kernel")
     ap.add_argument("--case", choices=sorted(CASES), default=None,
                     help="run only this workload's launches (for profilers)")
     return ap.parse_args()
@@ -355,6 +357,17 @@ def kernel_table(peaks: dict) -> dict:
     for K, N in ((4096, 6144), (4096, 28672), (14336, 4096)):
         for M in (1, 16, 128, 2048, 8192):
             out[f"linear_M{M}_K{K}_N{N}"] = gemm_entry(M, K, N, M + K + N, 0.02)
+    for M in (2048, 8192):  # Llama-3-8B gate/up (I = 14336) with the fused silu epilogue
+        K, inter = 4096, 14336
+        a = rand_bf16((M, K), 50 + M)
+        w = rand_bf16((K, 2 * inter), 51 + M, std=0.02)
+        o = torch.empty((M, inter), device="cuda", dtype=torch.bfloat16)
+        ms = graph_launch_ms([lambda: torch.ops.aot_kernel.gemm_silu_mul(o, a, w)])
+        tf = 2.0 * M * K * 2 * inter / (ms * 1e-3) / 1e12
+        out[f"gate_up_silu_M{M}_K{K}_I{inter}"] = {"ms": round(ms, 5), "tflops": round(tf, 2),
+                                                   "bound": "tensor",
+                                                   "frac": round(tf / peaks["bf16_tflops"], 4)}
+        del a, w, o
     torch.cuda.empty_cache()
 
     def hbm_entry(calls, nbytes, R):
@@ -391,21 +404,23 @@ def tp_mlp(args, rank: int, world: int, peaks: dict) -> dict:
     import torch
     import torch.distributed as dist
 
-    from aot_kernel.tp_mlp import MLPShard, TensorParallelMLP, shard_down, shard_gate_up
+    from aot_kernel.tp_mlp import (MLPShard, TensorParallelMLP, shard_down, shard_gate_up,
+                                   shard_gate_up_interleaved)
 
     T, H, inter = 4096, 8192, 28672
     x = rand_bf16((T, H), 30)
     nw = rand_bf16((H,), 31, std=0.1, mean=1.0)
     w_gu = rand_bf16((H, 2 * inter), 32, std=0.02)
-    wgu_r = shard_gate_up(w_gu, rank, world)
+    fused_silu = not args.tp_unfused_silu
+    wgu_r = (shard_gate_up_interleaved if fused_silu else shard_gate_up)(w_gu, rank, world)
     del w_gu
     w_d = rand_bf16((inter, H), 33, std=0.02)
     wd_r = shard_down(w_d, rank, world)
     del w_d
     torch.cuda.empty_cache()
     allreduce = args.tp_allreduce if world > 1 else "nccl"
-    block = TensorParallelMLP(MLPShard(nw, wgu_r, wd_r), eps=1e-6, chunks=args.tp_chunks,
-                              allreduce=allreduce)
+    block = TensorParallelMLP(MLPShard(nw, wgu_r, wd_r, fused_silu=fused_silu), eps=1e-6,
+                              chunks=args.tp_chunks, allreduce=allreduce)
     for _ in range(max(3, args.warmup)):
         block(x)
     torch.cuda.synchronize()
@@ -428,8 +443,9 @@ def tp_mlp(args, rank: int, world: int, peaks: dict) -> dict:
     per_gpu_ideal_ms = flops / world / (peaks["bf16_tflops"] * 1e12) * 1e3
     return {"tokens_per_s": T / (ms * 1e-3), "ms_per_step": ms, "tokens": T, "hidden": H,
             "intermediate": inter, "tp": world, "chunks": args.tp_chunks,
-            "allreduce": allreduce if world > 1 else None,
-            "gpu_launches_per_step": 4 if world == 1 or allreduce == "fused" else 3 + args.tp_chunks,
+            "allreduce": allreduce if world > 1 else None, "fused_silu": fused_silu,
+            "gpu_launches_per_step": (2 if fused_silu else 3)
+            + (1 if world == 1 or allreduce == "fused" else args.tp_chunks),
             "tensor_frac_per_gpu": per_gpu_ideal_ms / ms, "allreduce_bytes": T * H * 2,
             "phases_ms": phases}
 
@@ -443,7 +459,8 @@ def tp_phase_breakdown(block, x, world: int, reps: int = 5) -> dict:
 
     ops, s = block.ops, block.shard
     fused = world > 1 and block.allreduce == "fused"
-    names = ["rms_norm", "gemm_gate_up", "silu_mul"]
+    fsilu = s.fused_silu
+    names = ["rms_norm"] + (["gemm_gate_up+silu_mul (fused)"] if fsilu else ["gemm_gate_up", "silu_mul"])
     names += ["gemm_down+all_reduce (fused)"] if fused else ["gemm_down", "all_reduce"]
     acc = torch.zeros(len(names), dtype=torch.float64, device="cuda")
     for _ in range(reps):
@@ -452,22 +469,30 @@ def tp_phase_breakdown(block, x, world: int, reps: int = 5) -> dict:
             dist.barrier()
         torch.cuda.synchronize()
         torch.cuda._sleep(2_000_000)
-        ev[0].record()
+        i = 0
+        ev[i].record()
         h = ops.rms_norm(x, s.norm_weight, block.eps)
-        ev[1].record()
-        gu = ops.gemm(h, s.w_gate_up)
-        ev[2].record()
-        act = ops.silu_mul(gu[:, :block.inter_local], gu[:, block.inter_local:])
-        ev[3].record()
+        i += 1
+        ev[i].record()
+        if fsilu:
+            act = ops.gemm_silu_mul(h, s.w_gate_up)
+        else:
+            gu = ops.gemm(h, s.w_gate_up)
+            i += 1
+            ev[i].record()
+            act = ops.silu_mul(gu[:, :block.inter_local], gu[:, block.inter_local:])
+        i += 1
+        ev[i].record()
         if fused:
             block._fused(act, s.w_down)
-            ev[4].record()
         else:
             out = ops.gemm(act, s.w_down)
-            ev[4].record()
+            i += 1
+            ev[i].record()
             if world > 1:
                 dist.all_reduce(out)
-            ev[5].record()
+        i += 1
+        ev[i].record()
         torch.cuda.synchronize()
         acc += torch.tensor([ev[i].elapsed_time(ev[i + 1]) for i in range(len(names))],
                             dtype=torch.float64, device="cuda")

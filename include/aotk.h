@@ -169,6 +169,26 @@ AOTK_API int aotk_gemm_tc2(void* c, const void* a, const void* b, int64_t M, int
 AOTK_API int aotk_gemm_skinny(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
                      int dtype, void* stream);
 
+/* ---- gemm fused with silu(gate) * up ------------------------------------ */
+
+/* act[M, I] = silu(A @ W_gate) * (A @ W_up), fp32 accumulation, silu and
+ * product in fp32 from the accumulators, one rounding - the gate/up
+ * projection and the activation of a gated MLP in one kernel (the
+ * [M, 2I] gate/up product never reaches memory).  b_gate_up is [K, 2I]
+ * with W_gate and W_up interleaved in blocks of 128 columns:
+ * columns [256j, 256j + 128) = W_gate[:, 128j : 128j + 128], columns
+ * [256j + 128, 256j + 256) = W_up[:, 128j : 128j + 128]; I % 128 == 0,
+ * K % 8 == 0, FLOAT16/BFLOAT16, 16-byte aligned pointers.  M > 128 runs on
+ * the persistent tcgen05 kernel; a workspace of
+ * aotk_gemm_silu_mul_workspace_size bytes enables the K-split last wave as
+ * in aotk_gemm_opt_ws.  No reference counterpart (the reference composes
+ * ref.silu(a @ W_gate) * (a @ W_up)). */
+AOTK_API int aotk_gemm_silu_mul(void* act, const void* a, const void* b_gate_up, int64_t M,
+                                int64_t I, int64_t K, int dtype, void* workspace,
+                                size_t workspace_bytes, void* stream);
+AOTK_API int aotk_gemm_silu_mul_workspace_size(int64_t M, int64_t I, int64_t K, int dtype,
+                                               size_t* bytes);
+
 /* ---- gemm fused with the tensor-parallel all-reduce -------------------- */
 
 /* Buffers of one rank for aotk_gemm_allreduce.  `part` and the output are

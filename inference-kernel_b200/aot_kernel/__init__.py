@@ -9,7 +9,7 @@ is an alias of ``rmsnorm``; ``silu_mul`` and ``add_rmsnorm`` are new fused ops.
 """
 
 from .activation import relu, silu, silu_mul
-from .gemm import gemm, gemm_naive
+from .gemm import gemm, gemm_naive, gemm_silu_mul, interleave_gate_up
 from .norm import add_rmsnorm, rms_norm, rmsnorm
 
 __version__ = "0.1.0"
@@ -18,6 +18,8 @@ __all__ = [
     "add_rmsnorm",
     "gemm",
     "gemm_naive",
+    "gemm_silu_mul",
+    "interleave_gate_up",
     "relu",
     "rms_norm",
     "rmsnorm",

@@ -42,6 +42,8 @@ SIGNATURES: dict[str, list] = {
     "aotk_watchdog_status": [_int, ctypes.POINTER(ctypes.c_uint32), _int],
     "aotk_gemm_allreduce_tiles": [_i64, _i64, ctypes.POINTER(ctypes.c_int64)],
     "aotk_watchdog_selftest": [_ptr],
+    "aotk_gemm_silu_mul": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr, ctypes.c_size_t, _ptr],
+    "aotk_gemm_silu_mul_workspace_size": [_i64, _i64, _i64, _int, ctypes.POINTER(ctypes.c_size_t)],
     "aotk_gemm_allreduce": [_ptr, _ptr, _i64, _i64, _i64, _int, ctypes.c_void_p, _ptr],
 }
 
@@ -187,6 +189,18 @@ def gemm_tc2(c, a, b, M, N, K, dtype, stream=None) -> None:
 
 def gemm_skinny(c, a, b, M, N, K, dtype, stream=None) -> None:
     _gemm("aotk_gemm_skinny", c, a, b, M, N, K, dtype, stream)
+
+
+def gemm_silu_mul_workspace_size(M, I, K, dtype) -> int:
+    n = ctypes.c_size_t(0)
+    _call("aotk_gemm_silu_mul_workspace_size", M, I, K, dtype, ctypes.byref(n))
+    return n.value
+
+
+def gemm_silu_mul(act, a, b_gate_up, M, I, K, dtype, workspace=None, workspace_bytes=0,
+                  stream=None) -> None:
+    _call("aotk_gemm_silu_mul", _p(act), _p(a), _p(b_gate_up), M, I, K, dtype, _p(workspace),
+          workspace_bytes, _stream(stream))
 
 
 def gemm_allreduce_tiles(M: int, N: int) -> int:

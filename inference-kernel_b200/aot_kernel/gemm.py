@@ -49,3 +49,31 @@ def gemm_naive(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     out = torch.empty((a.size(0), b.size(1)), device=device, dtype=dtype)
     torch.ops.aot_kernel.gemm(out, a, b)
     return out
+
+
+GATE_UP_BLOCK = 128  # column block of the interleaved gate/up layout
+
+
+def interleave_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
+    """[K, I] gate and up weights -> the [K, 2I] layout ``gemm_silu_mul`` reads:
+    columns [256j, 256j+128) are gate block j, [256j+128, 256j+256) up block j."""
+    if w_gate.shape != w_up.shape or w_gate.dim() != 2:
+        raise ValueError("gate and up weights must be 2-D and of the same shape")
+    K, inter = w_gate.shape
+    if inter % GATE_UP_BLOCK:
+        raise ValueError(f"intermediate size {inter} is not a multiple of {GATE_UP_BLOCK}")
+    g = w_gate.reshape(K, inter // GATE_UP_BLOCK, 1, GATE_UP_BLOCK)
+    u = w_up.reshape(K, inter // GATE_UP_BLOCK, 1, GATE_UP_BLOCK)
+    return torch.cat([g, u], dim=2).reshape(K, 2 * inter).contiguous()
+
+
+def gemm_silu_mul(a: torch.Tensor, w_gate_up: torch.Tensor) -> torch.Tensor:
+    """silu(a @ W_gate) * (a @ W_up) in one kernel; ``w_gate_up`` from
+    ``interleave_gate_up``.  The gate/up product stays in TMEM: silu and the
+    product use the fp32 accumulators and the result is rounded once."""
+    device, dtype = _validate(a, w_gate_up)
+    if dtype not in _TENSOR_CORE_DTYPES:
+        raise ValueError(f"gemm_silu_mul supports fp16/bf16, got {dtype}")
+    out = torch.empty((a.size(0), w_gate_up.size(1) // 2), device=device, dtype=dtype)
+    torch.ops.aot_kernel.gemm_silu_mul(out, a, w_gate_up)
+    return out

@@ -11,7 +11,9 @@ With ``chunks > 1`` the token dimension is cut into slices whose all-reduce
 (asynchronous, on NCCL's stream) overlaps the down projection of the next
 slice.  With ``allreduce="fused"`` the down projection and the all-reduce are
 one kernel (``aotk_gemm_allreduce``): partial tiles are summed through
-NVSwitch multicast memory while the rest of the GEMM runs.
+NVSwitch multicast memory while the rest of the GEMM runs.  A shard built
+with ``fused_silu=True`` (``shard_gate_up_interleaved``) runs the gate/up
+projection and silu(gate) * up as one kernel (``gemm_silu_mul``).
 
 The reference has no multi-GPU code; its oracle for this block is the
 unsharded composition of ref.rmsnorm, ref.gemm and ref.silu.
@@ -27,9 +29,10 @@ import torch.distributed as dist
 
 
 def default_ops() -> SimpleNamespace:
-    from . import gemm, rms_norm, silu_mul
+    from . import gemm, gemm_silu_mul, rms_norm, silu_mul
 
-    return SimpleNamespace(rms_norm=rms_norm, gemm=gemm, silu_mul=silu_mul)
+    return SimpleNamespace(rms_norm=rms_norm, gemm=gemm, silu_mul=silu_mul,
+                           gemm_silu_mul=gemm_silu_mul)
 
 
 def shard_gate_up(w_gate_up: torch.Tensor, rank: int, world: int) -> torch.Tensor:
@@ -41,6 +44,15 @@ def shard_gate_up(w_gate_up: torch.Tensor, rank: int, world: int) -> torch.Tenso
     gate = w_gate_up[:, rank * s:(rank + 1) * s]
     up = w_gate_up[:, inter + rank * s: inter + (rank + 1) * s]
     return torch.cat([gate, up], dim=1).contiguous()
+
+
+def shard_gate_up_interleaved(w_gate_up: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Rank's gate/up shard in the interleaved layout of ``gemm_silu_mul``."""
+    from .gemm import interleave_gate_up
+
+    shard = shard_gate_up(w_gate_up, rank, world)
+    s = shard.shape[1] // 2
+    return interleave_gate_up(shard[:, :s], shard[:, s:])
 
 
 def shard_down(w_down: torch.Tensor, rank: int, world: int) -> torch.Tensor:
@@ -110,8 +122,9 @@ class FusedDownAllReduce:
 @dataclass
 class MLPShard:
     norm_weight: torch.Tensor  # [H]
-    w_gate_up: torch.Tensor    # [H, 2*I/W]
+    w_gate_up: torch.Tensor    # [H, 2*I/W]; interleaved in 128-column blocks when fused_silu
     w_down: torch.Tensor       # [I/W, H]
+    fused_silu: bool = False   # w_gate_up is in the gemm_silu_mul layout
 
 
 class TensorParallelMLP:
@@ -134,8 +147,11 @@ class TensorParallelMLP:
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         ops, s = self.ops, self.shard
         h = ops.rms_norm(x, s.norm_weight, self.eps)
-        gu = ops.gemm(h, s.w_gate_up)
-        act = ops.silu_mul(gu[:, :self.inter_local], gu[:, self.inter_local:])
+        if s.fused_silu:
+            act = ops.gemm_silu_mul(h, s.w_gate_up)
+        else:
+            gu = ops.gemm(h, s.w_gate_up)
+            act = ops.silu_mul(gu[:, :self.inter_local], gu[:, self.inter_local:])
         if self.world == 1:
             return ops.gemm(act, s.w_down)
         if self.allreduce == "fused":

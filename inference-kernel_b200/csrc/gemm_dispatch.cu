@@ -148,6 +148,29 @@ extern "C" int aotk_gemm_skinny(void* c, const void* a, const void* b, int64_t M
   return aotk::gemm_skinny(c, a, b, M, N, K, dtype, stream);
 }
 
+extern "C" int aotk_gemm_silu_mul_workspace_size(int64_t M, int64_t I, int64_t K, int dtype,
+                                                 size_t* bytes) {
+  using namespace aotk;
+  if (!bytes) return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_gemm_silu_mul_workspace_size: null pointer");
+  *bytes = 0;
+  if (M < 0 || I < 0 || K < 0)
+    return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_gemm_silu_mul_workspace_size: negative size");
+  if (dtype != AOTK_FLOAT16 && dtype != AOTK_BFLOAT16) return AOTK_OK;
+  DeviceInfo info;
+  if (int st = current_device_info(&info)) return st;
+  *bytes = gemm_tc_workspace_size(M, 2 * I, K, info.sm_count);
+  return AOTK_OK;
+}
+
+extern "C" int aotk_gemm_silu_mul(void* act, const void* a, const void* b_gate_up, int64_t M,
+                                  int64_t I, int64_t K, int dtype, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  using namespace aotk;
+  if (I < 0) return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_gemm_silu_mul: negative size");
+  if (M == 0 || I == 0) return AOTK_OK;
+  return gemm_silu_mul(act, a, b_gate_up, M, 2 * I, K, dtype, workspace, workspace_bytes, stream);
+}
+
 extern "C" int aotk_gemm_allreduce_tiles(int64_t M, int64_t N, int64_t* tiles) {
   using namespace aotk;
   if (!tiles || M < 0 || N < 0)

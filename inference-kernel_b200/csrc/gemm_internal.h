@@ -14,6 +14,12 @@ int gemm_tc(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t
             void* workspace, size_t ws_bytes, void* stream);
 size_t gemm_tc_workspace_size(int64_t M, int64_t N, int64_t K, int sm_count);
 
+// Persistent tcgen05 GEMM whose epilogue applies silu(gate) * up: b is
+// [K, N2] with gate and up interleaved in blocks of 128 columns, act is
+// [M, N2 / 2] (gemm_tc.cu).  Workspace as for gemm_tc with N = N2.
+int gemm_silu_mul(void* act, const void* a, const void* b, int64_t M, int64_t N2, int64_t K,
+                  int dtype, void* workspace, size_t ws_bytes, void* stream);
+
 // Persistent tcgen05 GEMM on CTA pairs, 256 x 256 tiles (gemm_tc2.cu).
 int gemm_tc2(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K, int dtype,
              void* stream);

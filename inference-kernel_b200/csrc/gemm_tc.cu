@@ -203,11 +203,23 @@ __device__ __forceinline__ void multimem_st16(uint64_t mc, const uint4& v) {
                : "memory");
 }
 
-template <typename T, int BN, int STAGES, bool kFused>
-__global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
+// Epilogue variants of the persistent kernel.
+enum : int {
+  kEpiStore = 0,      // C tile -> TMA store
+  kEpiAllReduce = 1,  // partial tile -> `part`, all-reduce warps (ArParams)
+  kEpiSiluMul = 2     // tile = [gate_j | up_j] (128 + 128 columns) -> silu(gate) * up, 128 columns
+};
+
+template <typename T, int BN, int STAGES, int kEpi>
+__global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, T* __restrict__ C, int M, int N, int K,
                    uint32_t idesc, TcSched sched, ArParams ar) {
+  constexpr bool kFused = kEpi == kEpiAllReduce;
+  constexpr bool kSiluMul = kEpi == kEpiSiluMul;
+  // Columns of C per tile and in total (the silu_mul epilogue halves both).
+  constexpr int kOutCols = kSiluMul ? BN / 2 : BN;
+  const int n_out = kSiluMul ? N / 2 : N;
   using L = TcLayout<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
@@ -396,8 +408,35 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
                             static_cast<uint32_t>(acc * BN);
       const int row_in_tile = q * 32 + lane;
       const int store_y = mb * kBM + q * 32;
+      bool whole_done = false;
+      if constexpr (kSiluMul) {
+        if (w.unit < 0) {
+          // Columns [0, BN/2) of the accumulator are gate, [BN/2, BN) up.
 #pragma unroll 1
-      for (int c = 0; c < BN / 64; ++c) {
+          for (int c = 0; c < BN / 128; ++c) {
+            uint32_t g[64], u[64];
+            tmem_ld_32x32b_x32(trow + c * 64, g);
+            tmem_ld_32x32b_x32(trow + c * 64 + 32, g + 32);
+            tmem_ld_32x32b_x32(trow + BN / 2 + c * 64, u);
+            tmem_ld_32x32b_x32(trow + BN / 2 + c * 64 + 32, u + 32);
+            tmem_wait_ld();
+            if (c == BN / 128 - 1) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(tempty_bar(acc));
+            }
+            const int store_x = nb * kOutCols + c * 64;
+            if (store_x >= n_out || store_y >= M) continue;
+            float f[64];
+#pragma unroll
+            for (int j = 0; j < 64; ++j) f[j] = silu_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
+            store_chunk(f, store_x, store_y);
+          }
+          whole_done = true;
+        }
+      }
+#pragma unroll 1
+      for (int c = 0; c < BN / 64 && !whole_done; ++c) {
         uint32_t r[64];
         tmem_ld_32x32b_x32(trow + c * 64, r);
         tmem_ld_32x32b_x32(trow + c * 64 + 32, r + 32);
@@ -457,35 +496,55 @@ __global__ void __launch_bounds__(kFused ? kThreadsFused : kThreads, 1)
             const int et = threadIdx.x - 64;  // 0..127
             const size_t unit_stride = static_cast<size_t>(kBM) * BN;
             const float* base = sched.ws + static_cast<size_t>(slot * sched.splits) * unit_stride;
-            constexpr int kF4 = kBM * BN / 4;
+            constexpr int kF4 = kBM * kOutCols / 4;  // float4 slots of the output tile
   #pragma unroll 1
             for (int f0 = et; f0 < kF4; f0 += 4 * 128) {
-              float4 sum[4];
+              float4 sum[4], sum_up[4];
   #pragma unroll
-              for (int u = 0; u < 4; ++u) sum[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+              for (int u = 0; u < 4; ++u) {
+                sum[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                sum_up[u] = sum[u];
+              }
               for (int sp = 0; sp < sched.splits; ++sp) {
-                float4 v[4];
+                const float* part = base + sp * unit_stride;
+                float4 v[4], vu[4];
   #pragma unroll
-                for (int u = 0; u < 4; ++u)
-                  v[u] = __ldcg(reinterpret_cast<const float4*>(base + sp * unit_stride) + f0 + u * 128);
+                for (int u = 0; u < 4; ++u) {
+                  const int f = f0 + u * 128;
+                  const float* p = part + (f / (kOutCols / 4)) * BN + (f % (kOutCols / 4)) * 4;
+                  v[u] = __ldcg(reinterpret_cast<const float4*>(p));
+                  if constexpr (kSiluMul) vu[u] = __ldcg(reinterpret_cast<const float4*>(p + BN / 2));
+                }
   #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                   sum[u].x += v[u].x;
                   sum[u].y += v[u].y;
                   sum[u].z += v[u].z;
                   sum[u].w += v[u].w;
+                  if constexpr (kSiluMul) {
+                    sum_up[u].x += vu[u].x;
+                    sum_up[u].y += vu[u].y;
+                    sum_up[u].z += vu[u].z;
+                    sum_up[u].w += vu[u].w;
+                  }
                 }
               }
   #pragma unroll
               for (int u = 0; u < 4; ++u) {
                 const int f = f0 + u * 128;
-                const int gr = mb * kBM + f / (BN / 4);
-                const int gc = nb * BN + (f % (BN / 4)) * 4;
-                if (gr < M && gc < N) {  // N % 8 == 0: gc < N implies gc + 3 < N
+                const int gr = mb * kBM + f / (kOutCols / 4);
+                const int gc = nb * kOutCols + (f % (kOutCols / 4)) * 4;
+                if constexpr (kSiluMul) {
+                  sum[u].x = silu_f(sum[u].x) * sum_up[u].x;
+                  sum[u].y = silu_f(sum[u].y) * sum_up[u].y;
+                  sum[u].z = silu_f(sum[u].z) * sum_up[u].z;
+                  sum[u].w = silu_f(sum[u].w) * sum_up[u].w;
+                }
+                if (gr < M && gc < n_out) {  // n_out % 8 == 0: gc < n_out implies gc + 3 < n_out
                   uint2 o;
                   o.x = Elem<T>::pack2(sum[u].x, sum[u].y);
                   o.y = Elem<T>::pack2(sum[u].z, sum[u].w);
-                  *reinterpret_cast<uint2*>(C + static_cast<size_t>(gr) * N + gc) = o;
+                  *reinterpret_cast<uint2*>(C + static_cast<size_t>(gr) * n_out + gc) = o;
                 }
               }
             }
@@ -628,12 +687,13 @@ TcPlan plan_tc(int M, int N, int K, int BN, int sms, bool allow_split) {
   return p;
 }
 
-template <typename T, int BN, int STAGES, bool kFused = false>
+template <typename T, int BN, int STAGES, int kEpi = kEpiStore>
 int launch_tc(void* c, const void* a, const void* b, int M, int N, int K, bool bf16,
               void* workspace, size_t ws_bytes, cudaStream_t stream, const DeviceInfo& info,
               const ArParams* ar = nullptr) {
   using L = TcLayout<BN, STAGES>;
-  auto kernel = gemm_tc_kernel<T, BN, STAGES, kFused>;
+  constexpr bool kFused = kEpi == kEpiAllReduce;
+  auto kernel = gemm_tc_kernel<T, BN, STAGES, kEpi>;
   if (int st = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), L::kAlloc, info)) return st;
   TcPlan p = plan_tc(M, N, K, BN, info.sm_count, workspace != nullptr);
   if (p.ws_bytes > 0 && (ws_bytes < p.ws_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255)))
@@ -648,7 +708,8 @@ int launch_tc(void* c, const void* a, const void* b, int M, int N, int K, bool b
   CUtensorMap ta, tb, tc;
   if (int st = make_tmap_2d_16bit(&ta, a, bf16, M, K, K, kBK, kBM)) return st;
   if (int st = make_tmap_2d_16bit(&tb, b, bf16, K, N, N, 64, kBK)) return st;
-  if (int st = make_tmap_2d_16bit(&tc, c, bf16, M, N, N, 64, 32)) return st;
+  const int n_out = kEpi == kEpiSiluMul ? N / 2 : N;
+  if (int st = make_tmap_2d_16bit(&tc, c, bf16, M, n_out, n_out, 64, 32)) return st;
   const uint32_t idesc = idesc_f16(bf16, kBM, BN, /*a_mn_major=*/false, /*b_mn_major=*/true);
   ArParams arp{};
   if (ar) arp = *ar;
@@ -677,9 +738,29 @@ int gemm_tc(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int m = (int)M, n = (int)N, k = (int)K;
   if (dtype == AOTK_BFLOAT16)
-    return launch_tc<__nv_bfloat16, kTcBN, kTcStages>(c, a, b, m, n, k, true, workspace, ws_bytes,
-                                                      s, info);
-  return launch_tc<__half, kTcBN, kTcStages>(c, a, b, m, n, k, false, workspace, ws_bytes, s, info);
+    return launch_tc<__nv_bfloat16, kTcBN, kTcStages, kEpiStore>(c, a, b, m, n, k, true, workspace,
+                                                                 ws_bytes, s, info);
+  return launch_tc<__half, kTcBN, kTcStages, kEpiStore>(c, a, b, m, n, k, false, workspace,
+                                                        ws_bytes, s, info);
+}
+
+int gemm_silu_mul(void* act, const void* a, const void* b, int64_t M, int64_t N2, int64_t K,
+                  int dtype, void* workspace, size_t ws_bytes, void* stream) {
+  DeviceInfo info;
+  if (int st = current_device_info(&info)) return st;
+  if (int st = require_sm100(info)) return st;
+  if (int st = check_tc_preconditions("aotk_gemm_silu_mul", act, a, b, M, N2, K, dtype)) return st;
+  if (N2 % kTcBN != 0)
+    return fail(AOTK_ERR_UNSUPPORTED,
+                "aotk_gemm_silu_mul: interleaved width 2*I = %lld must be a multiple of %d",
+                (long long)N2, kTcBN);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int m = (int)M, n = (int)N2, k = (int)K;
+  if (dtype == AOTK_BFLOAT16)
+    return launch_tc<__nv_bfloat16, kTcBN, kTcStages, kEpiSiluMul>(act, a, b, m, n, k, true,
+                                                                   workspace, ws_bytes, s, info);
+  return launch_tc<__half, kTcBN, kTcStages, kEpiSiluMul>(act, a, b, m, n, k, false, workspace,
+                                                          ws_bytes, s, info);
 }
 
 int gemm_allreduce_tiles(int64_t M, int64_t N) {
@@ -715,10 +796,10 @@ int gemm_allreduce(const void* a, const void* b, int64_t M, int64_t N, int64_t K
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int m = (int)M, n = (int)N, k = (int)K;
   if (dtype == AOTK_BFLOAT16)
-    return launch_tc<__nv_bfloat16, kTcBN, kTcStages, true>(bufs->part, a, b, m, n, k, true, nullptr,
-                                                            0, s, info, &ar);
-  return launch_tc<__half, kTcBN, kTcStages, true>(bufs->part, a, b, m, n, k, false, nullptr, 0, s,
-                                                   info, &ar);
+    return launch_tc<__nv_bfloat16, kTcBN, kTcStages, kEpiAllReduce>(bufs->part, a, b, m, n, k,
+                                                                     true, nullptr, 0, s, info, &ar);
+  return launch_tc<__half, kTcBN, kTcStages, kEpiAllReduce>(bufs->part, a, b, m, n, k, false,
+                                                            nullptr, 0, s, info, &ar);
 }
 
 int watchdog_selftest(void* stream) {

@@ -200,6 +200,35 @@ void gemm_opt(at::Tensor out, at::Tensor a, at::Tensor b) {
                op);
 }
 
+void gemm_silu_mul(at::Tensor out, at::Tensor a, at::Tensor b_gate_up) {
+  const char* op = "gemm_silu_mul";
+  check_cuda(a, op, "a");
+  check_cuda(b_gate_up, op, "b_gate_up");
+  check_cuda(out, op, "out");
+  check_same(a, b_gate_up, op, "a", "b_gate_up");
+  check_same(out, a, op, "out", "a");
+  TORCH_CHECK(a.dim() == 2 && b_gate_up.dim() == 2 && out.dim() == 2, "[", op, "] expects 2D tensors");
+  TORCH_CHECK(a.size(1) == b_gate_up.size(0), "[", op, "] inner dims mismatch: ", a.size(1), " vs ",
+              b_gate_up.size(0));
+  TORCH_CHECK(b_gate_up.size(1) % 2 == 0 && out.size(0) == a.size(0) &&
+                  out.size(1) == b_gate_up.size(1) / 2,
+              "[", op, "] out must be [M, N / 2] for b_gate_up [K, N]");
+  TORCH_CHECK(a.is_contiguous() && b_gate_up.is_contiguous() && out.is_contiguous(), "[", op,
+              "] tensors must be contiguous");
+  const int64_t M = a.size(0), K = a.size(1), I = out.size(1);
+  const int dtype = aotk_dtype(a, op);
+  c10::cuda::CUDAGuard guard(a.device());
+  size_t ws_bytes = 0;
+  check_status(aotk_gemm_silu_mul_workspace_size(M, I, K, dtype, &ws_bytes), op);
+  at::Tensor ws;
+  if (ws_bytes > 0)
+    ws = at::empty({static_cast<int64_t>(ws_bytes)}, a.options().dtype(at::kByte));
+  check_status(aotk_gemm_silu_mul(out.data_ptr(), a.data_ptr(), b_gate_up.data_ptr(), M, I, K, dtype,
+                                  ws_bytes > 0 ? ws.data_ptr() : nullptr, ws_bytes,
+                                  current_stream(a)),
+               op);
+}
+
 }  // namespace
 
 TORCH_LIBRARY(aot_kernel, m) {
@@ -225,6 +254,9 @@ TORCH_LIBRARY(aot_kernel, m) {
 
   m.def("gemm_opt(Tensor! out, Tensor a, Tensor b) -> ()");
   m.impl("gemm_opt", c10::kCUDA, &gemm_opt);
+
+  m.def("gemm_silu_mul(Tensor! out, Tensor a, Tensor b_gate_up) -> ()");
+  m.impl("gemm_silu_mul", c10::kCUDA, &gemm_silu_mul);
 }
 
 // `import aot_kernel._C` runs the static registration above; the module itself is empty.

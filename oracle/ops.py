@@ -110,6 +110,17 @@ def silu_mul_composed(gate: np.ndarray, up: np.ndarray, dtype: str) -> np.ndarra
     return round_to(silu(gate, dtype) * np.asarray(up, dtype=np.float32), dtype)
 
 
+def gemm_silu_mul(a: np.ndarray, w_gate: np.ndarray, w_up: np.ndarray, dtype: str) -> np.ndarray:
+    """silu(a @ W_gate) * (a @ W_up) with both products and the activation in
+    fp32 and one rounding (the fused gate/up kernel's contract; the reference
+    composes ref.silu(ref.gemm(a, W_gate)) * ref.gemm(a, W_up), rounding each
+    step)."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    g = a @ np.ascontiguousarray(w_gate, dtype=np.float32)
+    u = a @ np.ascontiguousarray(w_up, dtype=np.float32)
+    return round_to(_silu_f32(g) * u, dtype)
+
+
 def mlp_block(x, norm_w, w_gate_up, w_down, eps: float, dtype: str) -> np.ndarray:
     """Unsharded Llama MLP block as a composition of the ops above:
     rms_norm -> x @ [W_gate | W_up] -> silu(gate) * up -> @ W_down.

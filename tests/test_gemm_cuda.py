@@ -248,3 +248,34 @@ def test_split_and_whole_schedules_agree():
     torch.cuda.synchronize()
     diff = (whole.float() - split.float()).abs().max().item()
     assert diff <= 2e-2 * whole.float().abs().max().item()
+
+
+# ---- gate/up GEMM fused with silu(gate) * up ----
+
+@pytest.mark.parametrize("shape", [(256, 512, 256), (300, 328, 384), (2560, 1024, 1024),
+                                   (4096, 8192, 3584)], ids=str)
+def test_gemm_silu_mul_matches_oracle(shape):
+    """(M, K, I): interleaved [K, 2I] weight, act [M, I]; the last two shapes
+    leave a partial last wave (K-split path with the fused finalize)."""
+    import torch
+
+    import aot_kernel
+
+    M, K, inter = shape
+    a = randn((M, K), M + 1, "bfloat16")
+    wg = randn((K, inter), K + 2, "bfloat16", std=K ** -0.5)
+    wu = randn((K, inter), K + 3, "bfloat16", std=K ** -0.5)
+    ta = to_device(a, "bfloat16")
+    w = aot_kernel.interleave_gate_up(to_device(wg, "bfloat16"), to_device(wu, "bfloat16"))
+    act = aot_kernel.gemm_silu_mul(ta, w)
+    torch.cuda.synchronize()
+    rows = np.unique(np.concatenate([np.random.default_rng(2).integers(0, M, size=48),
+                                     np.arange(max(0, M - 128), M, 9)]))
+    expect = ops.gemm_silu_mul(a[rows], wg, wu, "bfloat16")
+    got = act[torch.as_tensor(rows, device="cuda")]
+    assert_close_for_gemm(got, expect, "bfloat16")
+    # agrees with the unfused composition within the GEMM tolerance
+    gate = aot_kernel.gemm(ta, to_device(wg, "bfloat16"))
+    up = aot_kernel.gemm(ta, to_device(wu, "bfloat16"))
+    ref2 = aot_kernel.silu_mul(gate, up)
+    assert_close_for_gemm(act, ref2, "bfloat16")

@@ -48,14 +48,17 @@ def _rank_main(rank: int, world: int, port: int, chunks: int, out_dir: str,
     import torch
     import torch.distributed as dist
 
-    from aot_kernel.tp_mlp import MLPShard, TensorParallelMLP, shard_down, shard_gate_up
+    from aot_kernel.tp_mlp import (MLPShard, TensorParallelMLP, shard_down, shard_gate_up,
+                                   shard_gate_up_interleaved)
 
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
                             device_id=dev)
     x, nw, wgu, wd = (torch.from_numpy(a).to(dev, torch.bfloat16) for a in _weights())
-    block = TensorParallelMLP(MLPShard(nw, shard_gate_up(wgu, rank, world), shard_down(wd, rank, world)),
+    fused_silu = allreduce == "fused"  # the fused runs also take the fused gate/up + silu path
+    wgu_r = (shard_gate_up_interleaved if fused_silu else shard_gate_up)(wgu, rank, world)
+    block = TensorParallelMLP(MLPShard(nw, wgu_r, shard_down(wd, rank, world), fused_silu=fused_silu),
                               chunks=chunks, allreduce=allreduce)
     y = block(x)
     y = block(x).clone()  # second call: epoch 2 of the fused path
@@ -77,13 +80,16 @@ def _check(y: np.ndarray, world: int) -> None:
     assert err <= 2e-2 * np.abs(full).max(), f"W={world}: max|err| {err} vs max|ref| {np.abs(full).max()}"
 
 
-def test_block_single_gpu():
+@pytest.mark.parametrize("fused_silu", [False, True])
+def test_block_single_gpu(fused_silu):
     import torch
 
-    from aot_kernel.tp_mlp import MLPShard, TensorParallelMLP
+    from aot_kernel.tp_mlp import MLPShard, TensorParallelMLP, shard_gate_up_interleaved
 
     x, nw, wgu, wd = (torch.from_numpy(a).to("cuda", torch.bfloat16) for a in _weights())
-    y = TensorParallelMLP(MLPShard(nw, wgu, wd))(x)
+    if fused_silu:
+        wgu = shard_gate_up_interleaved(wgu, 0, 1)
+    y = TensorParallelMLP(MLPShard(nw, wgu, wd, fused_silu=fused_silu))(x)
     torch.cuda.synchronize()
     _check(y.float().cpu().numpy(), 1)
 
