@@ -57,6 +57,9 @@ CASES = {
     "gemm_decode_m1": ("gemm", (1, 4096, 28672)),
     "gemm_decode_m16": ("gemm", (16, 4096, 28672)),
     "gemm_m128_down": ("gemm", (128, 14336, 4096)),
+    "scaled_gemm_fp8_8192": ("scaled_gemm_e4m3", (8192, 8192, 8192)),
+    "scaled_gemm_fp8_4096": ("scaled_gemm_e4m3", (4096, 4096, 4096)),
+    "scaled_gemm_int8_4096": ("scaled_gemm_int8", (4096, 4096, 4096)),
     "rms_norm": ("rms_norm", (8192, 4096)),
     "add_rms_norm": ("add_rms_norm", (8192, 4096)),
     "silu": ("silu", (8192, 14336)),
@@ -190,6 +193,28 @@ def rand_bf16(shape, seed: int, std: float = 1.0, mean: float = 0.0):
     if mean != 0.0:
         x.add_(mean)
     return x.to(torch.bfloat16)
+
+
+def rand_q(shape, seed: int, qdtype: str):
+    """8-bit GEMM operands drawn as the reference's scaled-GEMM benchmark draws
+    them: N(0, 1) converted to float8_e4m3fn, or integers in [-8, 8)."""
+    import torch
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    if qdtype == "int8":
+        return torch.randint(-8, 8, shape, generator=g, device="cuda", dtype=torch.int8)
+    return torch.randn(shape, generator=g, device="cuda").to(torch.float8_e4m3fn)
+
+
+def row_scales(M: int, N: int, seed: int):
+    import torch
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    sa = torch.rand(M, generator=g, device="cuda") * 0.1 + 0.01
+    sb = torch.rand(N, generator=g, device="cuda") * 0.1 + 0.01
+    return sa, sb
 
 
 def headline_gemm(args, rank: int, world: int, peaks: dict):
@@ -369,6 +394,50 @@ def kernel_table(peaks: dict) -> dict:
                                                    "frac": round(tf / peaks["bf16_tflops"], 4)}
         del a, w, o
     torch.cuda.empty_cache()
+
+    # 8-bit scaled GEMM (rowwise scales, bf16 out) beside the library kernel
+    # for the same operation on the same box: cuBLASLt fp8 through
+    # torch._scaled_mm (B column-major, as it requires) and torch._int_mm plus
+    # a dequantising multiply for int8 - the baselines of the reference's
+    # benchmarks/gemm/bench_scaled_gemm.py.
+    def scaled_entry(n, qdtype, seed):
+        M = K = N = n
+        R = _sets_for(M * K + K * N)
+        sets = [(rand_q((M, K), seed + 2 * i, qdtype), rand_q((K, N), seed + 2 * i + 1, qdtype))
+                for i in range(R)]
+        sa, sb = row_scales(M, N, seed + 99)
+        outs = [torch.empty((M, N), device="cuda", dtype=torch.bfloat16) for _ in range(R)]
+        calls = [lambda a=a, b=b, c=c: torch.ops.aot_kernel.scaled_gemm(c, a, b, sa, sb, True)
+                 for (a, b), c in zip(sets, outs)]
+        ms = graph_launch_ms(calls)
+        tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+        entry = {"ms": round(ms, 5), "tflops": round(tf, 2), "bound": "tensor", "input_sets": R}
+        cols = [b.t().contiguous().t() for _, b in sets]  # [K, N] views of [N, K] storage
+        del outs, calls
+        try:
+            if qdtype == "int8":
+                lib = [lambda a=a, bc=bc: (torch._int_mm(a, bc).float() * sa[:, None] * sb[None, :])
+                       .to(torch.bfloat16) for (a, _), bc in zip(sets, cols)]
+                name = "torch._int_mm + dequant"
+            else:
+                sa2, sb2 = sa.reshape(M, 1), sb.reshape(1, N)
+                lib = [lambda a=a, bc=bc: torch._scaled_mm(a, bc, scale_a=sa2, scale_b=sb2,
+                                                           out_dtype=torch.bfloat16)
+                       for (a, _), bc in zip(sets, cols)]
+                name = "torch._scaled_mm (cuBLASLt)"
+            lms = graph_launch_ms(lib)
+            ltf = 2.0 * M * N * K / (lms * 1e-3) / 1e12
+            entry["library"] = {"name": name, "ms": round(lms, 5), "tflops": round(ltf, 2)}
+            entry["frac_of_library"] = round(tf / ltf, 4)
+        except (RuntimeError, TypeError) as e:  # library path unavailable for this layout
+            entry["library"] = {"unavailable": str(e).splitlines()[0][:160]}
+        del sets, cols
+        torch.cuda.empty_cache()
+        return entry
+
+    for n in (4096, 8192):
+        out[f"scaled_gemm_fp8_{n}^3"] = scaled_entry(n, "e4m3", 70 + n)
+        out[f"scaled_gemm_int8_{n}^3"] = scaled_entry(n, "int8", 80 + n)
 
     def hbm_entry(calls, nbytes, R):
         ms = graph_launch_ms(calls)
@@ -603,6 +672,12 @@ def run_case(args) -> None:
         a = rand_bf16((M, K), 1)
         b = rand_bf16((K, N), 2, std=0.02)
         fn = lambda: aot_kernel.gemm(a, b)  # noqa: E731
+    elif kind.startswith("scaled_gemm"):
+        M, K, N = shape
+        q = kind.rsplit("_", 1)[1]
+        a, b = rand_q((M, K), 1, q), rand_q((K, N), 2, q)
+        sa, sb = row_scales(M, N, 3)
+        fn = lambda: aot_kernel.scaled_gemm(a, b, sa, sb)  # noqa: E731
     elif kind == "rms_norm":
         x = rand_bf16(shape, 3)
         w = rand_bf16((shape[1],), 4, std=0.1, mean=1.0)

@@ -36,11 +36,20 @@
 extern "C" {
 #endif
 
-/* Element types. */
+/* Element types.  The 8-bit types are inputs of aotk_scaled_gemm only. */
 enum aotk_dtype {
   AOTK_FLOAT32 = 0,
   AOTK_FLOAT16 = 1,
-  AOTK_BFLOAT16 = 2
+  AOTK_BFLOAT16 = 2,
+  AOTK_FLOAT8_E4M3 = 3, /* OCP e4m3 "fn": bias 7, no infinities, 0x7F / 0xFF NaN */
+  AOTK_INT8 = 4,
+  AOTK_FLOAT8_E5M2 = 5  /* OCP e5m2: bias 15, IEEE-style infinities and NaNs */
+};
+
+/* Granularity of the dequantisation scales of aotk_scaled_gemm. */
+enum aotk_scale_mode {
+  AOTK_SCALE_TENSOR = 0, /* scale_a and scale_b each hold one fp32 value */
+  AOTK_SCALE_ROW = 1     /* scale_a[M] per row of A, scale_b[N] per column of B */
 };
 
 /* Status codes returned by every entry point. */
@@ -188,6 +197,40 @@ AOTK_API int aotk_gemm_silu_mul(void* act, const void* a, const void* b_gate_up,
                                 size_t workspace_bytes, void* stream);
 AOTK_API int aotk_gemm_silu_mul_workspace_size(int64_t M, int64_t I, int64_t K, int dtype,
                                                size_t* bytes);
+
+/* ---- scaled (dequantising) 8-bit gemm ----------------------------------- */
+
+/* C[M, N] = (acc[m, n] * scale_a[m]) * scale_b[n] rounded once to out_dtype,
+ * acc = A[M, K] * B[K, N] with A and B both FLOAT8_E4M3 or both FLOAT8_E5M2
+ * (fp32 accumulation) or both INT8 (exact integer accumulation, converted to
+ * fp32).  scale_a /
+ * scale_b are dense fp32 device vectors of 1 value each (AOTK_SCALE_TENSOR)
+ * or M and N values (AOTK_SCALE_ROW).  out_dtype BFLOAT16, FLOAT16 or
+ * FLOAT32.  K % 16 == 0, N % 16 == 0 and 16-byte aligned A, B, C, scale_b
+ * run on the persistent tcgen05 kernel (kind::f8f6f4 / kind::i8, 128 x 256
+ * tiles, the scales applied to the TMEM accumulator in the epilogue); other
+ * shapes on a SIMT kernel.  A workspace of aotk_scaled_gemm_workspace_size
+ * bytes enables the K-split last wave as in aotk_gemm_opt_ws (NULL / 0: none).
+ * Replaces scaled_gemm(a, b, scale_a, scale_b, out_dtype, optimized)
+ * (jit_kernel/gemm.py:199-248; kernels jit_kernel/gemm.py:86-123 and
+ * 144-196: fp32 accumulator, acc * scale_a[:, None] * scale_b[None, :]). */
+AOTK_API int aotk_scaled_gemm(void* c, const void* a, const void* b, const float* scale_a,
+                              const float* scale_b, int64_t M, int64_t N, int64_t K, int in_dtype,
+                              int out_dtype, int scale_mode, void* workspace,
+                              size_t workspace_bytes, void* stream);
+AOTK_API int aotk_scaled_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int in_dtype,
+                                             size_t* bytes);
+
+/* Path-pinned variants of aotk_scaled_gemm: the tcgen05 kernel (returns
+ * AOTK_ERR_UNSUPPORTED where its preconditions do not hold) and the SIMT
+ * kernel (every shape). */
+AOTK_API int aotk_scaled_gemm_tc(void* c, const void* a, const void* b, const float* scale_a,
+                                 const float* scale_b, int64_t M, int64_t N, int64_t K,
+                                 int in_dtype, int out_dtype, int scale_mode, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+AOTK_API int aotk_scaled_gemm_simt(void* c, const void* a, const void* b, const float* scale_a,
+                                   const float* scale_b, int64_t M, int64_t N, int64_t K,
+                                   int in_dtype, int out_dtype, int scale_mode, void* stream);
 
 /* ---- gemm fused with the tensor-parallel all-reduce -------------------- */
 

@@ -5,11 +5,13 @@ Importing the package loads ``_C`` (the torch operator library, built in place
 by ``inference-kernel_b200/build.py``), which registers ``torch.ops.aot_kernel.*``
 and pulls in ``libaotk.so`` (the CUDA kernels and their C ABI).  Names and
 signatures follow the reference's ``aot_kernel/__init__.py:8-20``; ``rms_norm``
-is an alias of ``rmsnorm``; ``silu_mul`` and ``add_rmsnorm`` are new fused ops.
+is an alias of ``rmsnorm``; ``silu_mul``, ``add_rmsnorm`` and ``gemm_silu_mul``
+are new fused ops; ``scaled_gemm`` is the reference's 8-bit GEMM
+(``jit_kernel.gemm.scaled_gemm``, a Triton kernel there) with the same signature.
 """
 
 from .activation import relu, silu, silu_mul
-from .gemm import gemm, gemm_naive, gemm_silu_mul, interleave_gate_up
+from .gemm import gemm, gemm_naive, gemm_silu_mul, interleave_gate_up, scaled_gemm
 from .norm import add_rmsnorm, rms_norm, rmsnorm
 
 __version__ = "0.1.0"
@@ -23,6 +25,7 @@ __all__ = [
     "relu",
     "rms_norm",
     "rmsnorm",
+    "scaled_gemm",
     "silu",
     "silu_mul",
 ]

@@ -16,6 +16,8 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "libaotk.so"
 
 FLOAT32, FLOAT16, BFLOAT16 = 0, 1, 2
+FLOAT8_E4M3, INT8, FLOAT8_E5M2 = 3, 4, 5  # inputs of aotk_scaled_gemm
+SCALE_TENSOR, SCALE_ROW = 0, 1
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_CUDA, ERR_DEVICE = 0, 1, 2, 3, 4
 
 _i64 = ctypes.c_int64
@@ -45,6 +47,13 @@ SIGNATURES: dict[str, list] = {
     "aotk_gemm_silu_mul": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr, ctypes.c_size_t, _ptr],
     "aotk_gemm_silu_mul_workspace_size": [_i64, _i64, _i64, _int, ctypes.POINTER(ctypes.c_size_t)],
     "aotk_gemm_allreduce": [_ptr, _ptr, _i64, _i64, _i64, _int, ctypes.c_void_p, _ptr],
+    "aotk_scaled_gemm": [_ptr, _ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _int, _int, _ptr,
+                         ctypes.c_size_t, _ptr],
+    "aotk_scaled_gemm_workspace_size": [_i64, _i64, _i64, _int, ctypes.POINTER(ctypes.c_size_t)],
+    "aotk_scaled_gemm_tc": [_ptr, _ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _int, _int, _ptr,
+                            ctypes.c_size_t, _ptr],
+    "aotk_scaled_gemm_simt": [_ptr, _ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _int, _int,
+                              _ptr],
 }
 
 
@@ -94,7 +103,14 @@ def load(path: str | Path | None = None) -> ctypes.CDLL:
 def dtype_code(dtype) -> int:
     import torch
 
-    return {torch.float32: FLOAT32, torch.float16: FLOAT16, torch.bfloat16: BFLOAT16}[dtype]
+    return {
+        torch.float32: FLOAT32,
+        torch.float16: FLOAT16,
+        torch.bfloat16: BFLOAT16,
+        torch.float8_e4m3fn: FLOAT8_E4M3,
+        torch.float8_e5m2: FLOAT8_E5M2,
+        torch.int8: INT8,
+    }[dtype]
 
 
 def _p(x) -> int | None:
@@ -201,6 +217,30 @@ def gemm_silu_mul(act, a, b_gate_up, M, I, K, dtype, workspace=None, workspace_b
                   stream=None) -> None:
     _call("aotk_gemm_silu_mul", _p(act), _p(a), _p(b_gate_up), M, I, K, dtype, _p(workspace),
           workspace_bytes, _stream(stream))
+
+
+def scaled_gemm_workspace_size(M, N, K, in_dtype) -> int:
+    n = ctypes.c_size_t(0)
+    _call("aotk_scaled_gemm_workspace_size", M, N, K, in_dtype, ctypes.byref(n))
+    return n.value
+
+
+def scaled_gemm(c, a, b, scale_a, scale_b, M, N, K, in_dtype, out_dtype, scale_mode,
+                workspace=None, workspace_bytes=0, stream=None) -> None:
+    _call("aotk_scaled_gemm", _p(c), _p(a), _p(b), _p(scale_a), _p(scale_b), M, N, K, in_dtype,
+          out_dtype, scale_mode, _p(workspace), workspace_bytes, _stream(stream))
+
+
+def scaled_gemm_tc(c, a, b, scale_a, scale_b, M, N, K, in_dtype, out_dtype, scale_mode,
+                   workspace=None, workspace_bytes=0, stream=None) -> None:
+    _call("aotk_scaled_gemm_tc", _p(c), _p(a), _p(b), _p(scale_a), _p(scale_b), M, N, K, in_dtype,
+          out_dtype, scale_mode, _p(workspace), workspace_bytes, _stream(stream))
+
+
+def scaled_gemm_simt(c, a, b, scale_a, scale_b, M, N, K, in_dtype, out_dtype, scale_mode,
+                     stream=None) -> None:
+    _call("aotk_scaled_gemm_simt", _p(c), _p(a), _p(b), _p(scale_a), _p(scale_b), M, N, K,
+          in_dtype, out_dtype, scale_mode, _stream(stream))
 
 
 def gemm_allreduce_tiles(M: int, N: int) -> int:

@@ -1,4 +1,5 @@
-"""GEMM wrappers: ``gemm`` (tensor-core path) and ``gemm_naive`` (SIMT path).
+"""GEMM wrappers: ``gemm`` (tensor-core path), ``gemm_naive`` (SIMT path),
+the fused ``gemm_silu_mul`` and the 8-bit ``scaled_gemm``.
 
 Mirrors aot_kernel/gemm.py:22-51 of the reference: validate, allocate ``out``,
 call the registered op.  ``gemm`` sends fp16/bf16 to ``gemm_opt``, which picks
@@ -76,4 +77,62 @@ def gemm_silu_mul(a: torch.Tensor, w_gate_up: torch.Tensor) -> torch.Tensor:
         raise ValueError(f"gemm_silu_mul supports fp16/bf16, got {dtype}")
     out = torch.empty((a.size(0), w_gate_up.size(1) // 2), device=device, dtype=dtype)
     torch.ops.aot_kernel.gemm_silu_mul(out, a, w_gate_up)
+    return out
+
+
+_SCALED_INPUT_DTYPES = (torch.float8_e4m3fn, torch.float8_e5m2, torch.int8)
+
+
+def scaled_gemm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    scale_a: torch.Tensor,
+    scale_b: torch.Tensor,
+    out_dtype: torch.dtype = torch.bfloat16,
+    optimized: bool = True,
+) -> torch.Tensor:
+    """C = (A @ B) * scale_a * scale_b for quantised 8-bit A [M, K] and B [K, N].
+
+    Same signature, checks and error types as the reference's
+    ``jit_kernel.gemm.scaled_gemm`` (jit_kernel/gemm.py:199-248): A and B are
+    both float8_e4m3fn, both float8_e5m2 or both int8; the scales are float32
+    and either tensorwise (one value each) or rowwise (``scale_a.numel() == M``,
+    ``scale_b.numel() == N``), anything else is a ValueError.  The product is
+    accumulated in fp32 (int8: exactly, in int32), scaled as
+    ``(acc * scale_a[m]) * scale_b[n]`` and rounded once to ``out_dtype``
+    (bfloat16, float16 or float32).  ``optimized=True`` runs the tcgen05
+    kernel (kind::f8f6f4 / kind::i8) where K and N are multiples of 16, the
+    SIMT kernel otherwise; ``optimized=False`` always runs the SIMT kernel.
+    """
+    if a.dim() != 2 or b.dim() != 2:
+        raise AssertionError("gemm expects 2D inputs")
+    assert_is_cuda(a, b)
+    assert_contiguous(a, b)
+    device = assert_same_device(a, b)
+    dtype = assert_same_dtype(a, b)
+    M, K1 = a.shape
+    K2, N = b.shape
+    if K1 != K2:
+        raise AssertionError("gemm shape mismatch")
+    assert_is_cuda(scale_a, scale_b)
+    if scale_a.dtype != torch.float32 or scale_b.dtype != torch.float32:
+        raise AssertionError("scales must be float32")
+    if dtype not in _SCALED_INPUT_DTYPES:
+        raise ValueError(
+            f"scaled_gemm expects float8_e4m3fn, float8_e5m2 or int8 inputs, got {dtype}"
+        )
+    sa_n, sb_n = scale_a.numel(), scale_b.numel()
+    if not ((sa_n == 1 and sb_n == 1) or (sa_n == M and sb_n == N)):
+        raise ValueError(
+            "expect tensorwise (scalar scale_a and scale_b) "
+            "or rowwise (scale_a.numel()==M, scale_b.numel()==N)"
+        )
+    if scale_a.device != device or scale_b.device != device:
+        raise ValueError(
+            f"device mismatch: scales on {scale_a.device} / {scale_b.device}, inputs on {device}"
+        )
+    out = torch.empty((M, N), device=device, dtype=out_dtype)
+    sa = scale_a.reshape(-1).contiguous()
+    sb = scale_b.reshape(-1).contiguous()
+    torch.ops.aot_kernel.scaled_gemm(out, a, b, sa, sb, bool(optimized))
     return out

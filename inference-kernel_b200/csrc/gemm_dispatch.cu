@@ -6,6 +6,8 @@
 //                                          (decode; HBM-bound on the weight)
 //   16-bit, TMA-addressable, M > 128   -> persistent tcgen05 kernel
 //   anything else                       -> SIMT kernel
+// aotk_scaled_gemm (8-bit inputs): K % 16 == 0, N % 16 == 0, aligned -> the
+// persistent kernel on kind::f8f6f4 / kind::i8, else its SIMT kernel.
 // The reference routes in its Python wrapper instead: fp16/bf16 with
 // K % 16 == 0 to gemm_opt, everything else to the naive tier
 // (aot_kernel/gemm.py:39-42).
@@ -169,6 +171,108 @@ extern "C" int aotk_gemm_silu_mul(void* act, const void* a, const void* b_gate_u
   if (I < 0) return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_gemm_silu_mul: negative size");
   if (M == 0 || I == 0) return AOTK_OK;
   return gemm_silu_mul(act, a, b_gate_up, M, 2 * I, K, dtype, workspace, workspace_bytes, stream);
+}
+
+namespace aotk {
+namespace {
+
+bool scaled_in_dtype(int d) {
+  return d == AOTK_FLOAT8_E4M3 || d == AOTK_FLOAT8_E5M2 || d == AOTK_INT8;
+}
+
+int validate_scaled(const char* who, const void* c, const void* a, const void* b, const float* sa,
+                    const float* sb, int64_t M, int64_t N, int64_t K, int in_dtype, int out_dtype,
+                    int scale_mode) {
+  if (M < 0 || N < 0 || K < 0)
+    return fail(AOTK_ERR_INVALID_ARGUMENT, "%s: negative size (M=%lld N=%lld K=%lld)", who,
+                (long long)M, (long long)N, (long long)K);
+  if (!scaled_in_dtype(in_dtype))
+    return fail(AOTK_ERR_UNSUPPORTED, "%s: input dtype %d is not FLOAT8_E4M3, FLOAT8_E5M2 or INT8",
+                who, in_dtype);
+  if (!valid_dtype(out_dtype))
+    return fail(AOTK_ERR_UNSUPPORTED, "%s: unsupported output dtype %d", who, out_dtype);
+  if (scale_mode != AOTK_SCALE_TENSOR && scale_mode != AOTK_SCALE_ROW)
+    return fail(AOTK_ERR_INVALID_ARGUMENT, "%s: unknown scale mode %d", who, scale_mode);
+  if (M > 0 && N > 0 && (!c || !sa || !sb || (K > 0 && (!a || !b))))
+    return fail(AOTK_ERR_INVALID_ARGUMENT, "%s: null pointer", who);
+  return AOTK_OK;
+}
+
+// The tcgen05 kernel reads A / B rows through TMA (16-byte row strides: K and
+// N multiples of 16 bytes) and B's scales as float4.
+bool scaled_tc_eligible(const void* c, const void* a, const void* b, const float* sb, int64_t M,
+                        int64_t N, int64_t K, int scale_mode) {
+  if (K <= 0 || K % 16 != 0 || N % 16 != 0) return false;
+  if (M >= (1LL << 31) || N >= (1LL << 31) || K >= (1LL << 31)) return false;
+  if (scale_mode == AOTK_SCALE_ROW && !aligned16(sb)) return false;
+  return aligned16(a) && aligned16(b) && aligned16(c);
+}
+
+}  // namespace
+}  // namespace aotk
+
+extern "C" int aotk_scaled_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int in_dtype,
+                                               size_t* bytes) {
+  using namespace aotk;
+  if (!bytes) return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_scaled_gemm_workspace_size: null pointer");
+  *bytes = 0;
+  if (M < 0 || N < 0 || K < 0)
+    return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_scaled_gemm_workspace_size: negative size");
+  if (!scaled_in_dtype(in_dtype)) return AOTK_OK;
+  if (K % 16 != 0 || N % 16 != 0) return AOTK_OK;
+  DeviceInfo info;
+  if (int st = current_device_info(&info)) return st;
+  *bytes = gemm_scaled_tc_workspace_size(M, N, K, info.sm_count);
+  return AOTK_OK;
+}
+
+extern "C" int aotk_scaled_gemm_tc(void* c, const void* a, const void* b, const float* scale_a,
+                                   const float* scale_b, int64_t M, int64_t N, int64_t K,
+                                   int in_dtype, int out_dtype, int scale_mode, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+  using namespace aotk;
+  const char* who = "aotk_scaled_gemm_tc";
+  if (int st = validate_scaled(who, c, a, b, scale_a, scale_b, M, N, K, in_dtype, out_dtype,
+                               scale_mode))
+    return st;
+  if (M == 0 || N == 0 || K == 0)
+    return fail(AOTK_ERR_INVALID_ARGUMENT, "%s: empty problem (M=%lld N=%lld K=%lld)", who,
+                (long long)M, (long long)N, (long long)K);
+  if (!scaled_tc_eligible(c, a, b, scale_b, M, N, K, scale_mode))
+    return fail(AOTK_ERR_UNSUPPORTED,
+                "%s: needs K %% 16 == 0, N %% 16 == 0 and 16-byte aligned A, B, C and row scales "
+                "(M=%lld N=%lld K=%lld)",
+                who, (long long)M, (long long)N, (long long)K);
+  return gemm_scaled_tc(c, a, b, scale_a, scale_b, M, N, K, in_dtype, out_dtype, scale_mode,
+                        workspace, workspace_bytes, stream);
+}
+
+extern "C" int aotk_scaled_gemm_simt(void* c, const void* a, const void* b, const float* scale_a,
+                                     const float* scale_b, int64_t M, int64_t N, int64_t K,
+                                     int in_dtype, int out_dtype, int scale_mode, void* stream) {
+  using namespace aotk;
+  if (int st = validate_scaled("aotk_scaled_gemm_simt", c, a, b, scale_a, scale_b, M, N, K,
+                               in_dtype, out_dtype, scale_mode))
+    return st;
+  return gemm_scaled_simt(c, a, b, scale_a, scale_b, M, N, K, in_dtype, out_dtype, scale_mode,
+                          stream);
+}
+
+extern "C" int aotk_scaled_gemm(void* c, const void* a, const void* b, const float* scale_a,
+                                const float* scale_b, int64_t M, int64_t N, int64_t K, int in_dtype,
+                                int out_dtype, int scale_mode, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  using namespace aotk;
+  if (int st = validate_scaled("aotk_scaled_gemm", c, a, b, scale_a, scale_b, M, N, K, in_dtype,
+                               out_dtype, scale_mode))
+    return st;
+  if (M == 0 || N == 0) return AOTK_OK;
+  if (K == 0) return zero_output(c, M, N, out_dtype, stream);
+  if (scaled_tc_eligible(c, a, b, scale_b, M, N, K, scale_mode))
+    return gemm_scaled_tc(c, a, b, scale_a, scale_b, M, N, K, in_dtype, out_dtype, scale_mode,
+                          workspace, workspace_bytes, stream);
+  return gemm_scaled_simt(c, a, b, scale_a, scale_b, M, N, K, in_dtype, out_dtype, scale_mode,
+                          stream);
 }
 
 extern "C" int aotk_gemm_allreduce_tiles(int64_t M, int64_t N, int64_t* tiles) {

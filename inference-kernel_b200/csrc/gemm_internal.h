@@ -20,6 +20,20 @@ size_t gemm_tc_workspace_size(int64_t M, int64_t N, int64_t K, int sm_count);
 int gemm_silu_mul(void* act, const void* a, const void* b, int64_t M, int64_t N2, int64_t K,
                   int dtype, void* workspace, size_t ws_bytes, void* stream);
 
+// Persistent tcgen05 GEMM on 8-bit operands (e4m3 or int8, kind::f8f6f4 /
+// kind::i8) with the dequantisation epilogue C = (A * B) * scale_a * scale_b
+// (gemm_tc.cu).  The caller has checked shapes, alignment and dtypes
+// (scaled_tc_eligible); workspace as for gemm_tc.
+int gemm_scaled_tc(void* c, const void* a, const void* b, const float* scale_a,
+                   const float* scale_b, int64_t M, int64_t N, int64_t K, int in_dtype,
+                   int out_dtype, int scale_mode, void* workspace, size_t ws_bytes, void* stream);
+size_t gemm_scaled_tc_workspace_size(int64_t M, int64_t N, int64_t K, int sm_count);
+
+// SIMT scaled GEMM for every shape (gemm_scaled_simt.cu).
+int gemm_scaled_simt(void* c, const void* a, const void* b, const float* scale_a,
+                     const float* scale_b, int64_t M, int64_t N, int64_t K, int in_dtype,
+                     int out_dtype, int scale_mode, void* stream);
+
 // Persistent tcgen05 GEMM on CTA pairs, 256 x 256 tiles (gemm_tc2.cu).
 int gemm_tc2(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K, int dtype,
              void* stream);

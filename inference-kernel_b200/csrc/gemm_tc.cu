@@ -45,8 +45,6 @@ using namespace sm100;
 __device__ unsigned g_tc_watchdog;
 
 constexpr int kBM = 128;
-constexpr int kBK = 64;  // one 128-byte swizzle row of 16-bit elements
-constexpr int kUmmaK = 16;
 constexpr int kThreads = 192;       // plain GEMM: producer, MMA, 4 epilogue warps
 constexpr int kThreadsFused = 320;  // + 4 all-reduce warps (gemm_allreduce)
 constexpr int kGroupM = 16;  // M tiles per raster group
@@ -56,11 +54,62 @@ enum : unsigned { kWdProducer = 1u, kWdMma = 2u, kWdEpilogue = 4u, kWdPeer = 64u
 
 __device__ unsigned g_never_set;  // stays 0: the self-test's flag that nothing sets
 
-template <int BN, int STAGES>
+// Operand kinds: element size, the tcgen05 MMA that consumes them and its
+// instruction-descriptor formats.  A K block is one 128-byte swizzle row of
+// elements (kBK); one MMA consumes 32 bytes of it (kUmmaK elements).
+template <typename T>
+struct Op16 {
+  static constexpr int kBytes = 2;
+  static constexpr bool kIntAcc = false;
+  static constexpr uint32_t idesc(int m, int n) {
+    return idesc_f16(std::is_same<T, __nv_bfloat16>::value, m, n, false, true);
+  }
+  __device__ __forceinline__ static void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id,
+                                             bool acc) {
+    umma_f16(d, a, b, id, acc);
+  }
+};
+struct OpE4m3 {
+  static constexpr int kBytes = 1;
+  static constexpr bool kIntAcc = false;
+  static constexpr uint32_t idesc(int m, int n) { return idesc_make(1u, 0u, m, n, false, true); }
+  __device__ __forceinline__ static void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id,
+                                             bool acc) {
+    umma_f8f6f4(d, a, b, id, acc);
+  }
+};
+struct OpE5m2 {
+  static constexpr int kBytes = 1;
+  static constexpr bool kIntAcc = false;
+  static constexpr uint32_t idesc(int m, int n) { return idesc_make(1u, 1u, m, n, false, true); }
+  __device__ __forceinline__ static void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id,
+                                             bool acc) {
+    umma_f8f6f4(d, a, b, id, acc);
+  }
+};
+struct OpS8 {
+  static constexpr int kBytes = 1;
+  static constexpr bool kIntAcc = true;  // s32 accumulator
+  static constexpr uint32_t idesc(int m, int n) { return idesc_make(2u, 1u, m, n, false, true); }
+  __device__ __forceinline__ static void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id,
+                                             bool acc) {
+    umma_i8(d, a, b, id, acc);
+  }
+};
+
+template <int kInBytes>
+struct OpShape {
+  static constexpr int kBK = 128 / kInBytes;    // elements per K block
+  static constexpr int kUmmaK = 32 / kInBytes;  // elements per MMA
+};
+
+template <int BN, int STAGES, int kInBytes = 2>
 struct TcLayout {
-  static constexpr uint32_t kABytes = kBM * kBK * 2;
-  static constexpr uint32_t kBBox = kBK * 128;  // one 64 (N) x 64 (K) box
-  static constexpr uint32_t kBBytes = (BN / 64) * kBBox;
+  static constexpr int kBK = OpShape<kInBytes>::kBK;
+  static constexpr int kBoxN = 128 / kInBytes;  // N elements per B box
+  static constexpr uint32_t kABytes = kBM * 128;
+  static constexpr uint32_t kBBox = kBK * 128;  // one kBoxN (N) x kBK (K) box
+  static constexpr uint32_t kBBytes = (BN / kBoxN) * kBBox;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr uint32_t kCBuf = 32 * 128;  // 32 rows x 64 columns x 2 bytes
   static constexpr uint32_t kOffA = 0;
@@ -207,20 +256,56 @@ __device__ __forceinline__ void multimem_st16(uint64_t mc, const uint4& v) {
 enum : int {
   kEpiStore = 0,      // C tile -> TMA store
   kEpiAllReduce = 1,  // partial tile -> `part`, all-reduce warps (ArParams)
-  kEpiSiluMul = 2     // tile = [gate_j | up_j] (128 + 128 columns) -> silu(gate) * up, 128 columns
+  kEpiSiluMul = 2,    // tile = [gate_j | up_j] (128 + 128 columns) -> silu(gate) * up, 128 columns
+  kEpiScaled = 3      // C = (acc * scale_a[row]) * scale_b[col] (ScaleParams)
 };
 
-template <typename T, int BN, int STAGES, int kEpi>
+// Dequantisation scales of the scaled epilogue: fp32 vectors read with a step
+// of 0 (one scale for the whole operand) or 1 (one per row of A / column of B).
+struct ScaleParams {
+  const float* sa;
+  const float* sb;
+  int sa_step, sb_step;
+};
+
+// 16-bit or fp32 output element; stores and packs of 2 or 4 values.
+template <typename T>
+__device__ __forceinline__ void store4(T* p, float a, float b, float c, float d) {
+  if constexpr (std::is_same<T, float>::value) {
+    *reinterpret_cast<float4*>(p) = make_float4(a, b, c, d);
+  } else {
+    uint2 o;
+    o.x = Elem<T>::pack2(a, b);
+    o.y = Elem<T>::pack2(c, d);
+    *reinterpret_cast<uint2*>(p) = o;
+  }
+}
+
+// Scale factor of column `col` of B: four consecutive columns (col % 4 == 0).
+// Columns at or beyond n read as 0; n % 4 == 0, so a group is all in or out.
+__device__ __forceinline__ float4 load_sb4(const ScaleParams& sc, int col, int n) {
+  if (sc.sb_step == 0) {
+    const float v = __ldg(sc.sb);
+    return make_float4(v, v, v, v);
+  }
+  if (col >= n) return make_float4(0.f, 0.f, 0.f, 0.f);
+  return __ldg(reinterpret_cast<const float4*>(sc.sb + col));
+}
+
+template <typename Op, typename T, int BN, int STAGES, int kEpi>
 __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, T* __restrict__ C, int M, int N, int K,
-                   uint32_t idesc, TcSched sched, ArParams ar) {
+                   uint32_t idesc, TcSched sched, ArParams ar, ScaleParams sc) {
   constexpr bool kFused = kEpi == kEpiAllReduce;
   constexpr bool kSiluMul = kEpi == kEpiSiluMul;
+  constexpr bool kScaled = kEpi == kEpiScaled;
   // Columns of C per tile and in total (the silu_mul epilogue halves both).
   constexpr int kOutCols = kSiluMul ? BN / 2 : BN;
   const int n_out = kSiluMul ? N / 2 : N;
-  using L = TcLayout<BN, STAGES>;
+  using L = TcLayout<BN, STAGES, Op::kBytes>;
+  constexpr int kBK = L::kBK;
+  constexpr int kUmmaK = OpShape<Op::kBytes>::kUmmaK;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -289,8 +374,9 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
           mbar_arrive_expect_tx(fb, L::kStageBytes);
           tma_load_2d(sA + stage * L::kABytes, &tmA, kb * kBK, mb * kBM, fb);
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j) {
-            tma_load_2d(sB + stage * L::kBBytes + j * L::kBBox, &tmB, nb * BN + j * 64, kb * kBK, fb);
+          for (int j = 0; j < BN / L::kBoxN; ++j) {
+            tma_load_2d(sB + stage * L::kBBytes + j * L::kBBox, &tmB, nb * BN + j * L::kBoxN,
+                        kb * kBK, fb);
           }
           ++issued;
           if (++stage == STAGES) {
@@ -337,11 +423,11 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
           const uint32_t b0 = sB + stage * L::kBBytes;
 #pragma unroll
           for (int k = 0; k < kBK / kUmmaK; ++k) {
-            // A: K-major, advance 16 elements (32 B) inside the swizzle row.
-            // B: MN-major, advance 16 K rows (2 atoms of 8 rows x 128 B).
-            const uint64_t ad = sdesc_sw128(a0 + k * kUmmaK * 2, 16, 1024);
+            // A: K-major, advance 32 B inside the swizzle row.
+            // B: MN-major, advance kUmmaK K rows (atoms of 8 rows x 128 B).
+            const uint64_t ad = sdesc_sw128(a0 + k * 32, 16, 1024);
             const uint64_t bd = sdesc_sw128(b0 + k * kUmmaK * 128, L::kBBox, 1024);
-            umma_f16(d_tmem, ad, bd, idesc, kb > w.kb0 || k > 0);
+            Op::mma(d_tmem, ad, bd, idesc, kb > w.kb0 || k > 0);
           }
           umma_commit(empty_bar(stage));
           if (++stage == STAGES) {
@@ -369,31 +455,41 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
     uint32_t acc_phase = 0;
     int nstore = 0;
     const uint64_t c_policy = l2_policy_evict_first();
-    // Packs 64 fp32 values of this lane's row into 16-bit, stages them in a
-    // 128-byte-swizzled 32 x 64 box and TMA-stores the box at (x, y).
+    // Packs 64 fp32 values of this lane's row into T, stages them in
+    // 128-byte-swizzled boxes of 32 rows x 128 bytes (one box for 16-bit T,
+    // two for fp32) and TMA-stores each box at (x + its first column, y).
+    constexpr int kBoxCols = 128 / static_cast<int>(sizeof(T));
     auto store_chunk = [&](const float (&f)[64], int x, int y) {
-      uint32_t pk[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) pk[i] = Elem<T>::pack2(f[2 * i], f[2 * i + 1]);
-      const uint32_t buf = cbuf + (nstore & 1) * L::kCBuf;
-      if (nstore >= 2 && lane == 0) bulk_wait_read<1>();
-      __syncwarp();
-      // Row `lane` of the box, 16-byte chunk j stored at j ^ (row % 8).
-      const uint32_t row = buf + lane * 128;
+      for (int h = 0; h < 64 / kBoxCols; ++h) {
+        uint32_t pk[32];
+        if constexpr (sizeof(T) == 4) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        st_shared_v4(row + ((j ^ (lane & 7)) << 4), pk[4 * j], pk[4 * j + 1], pk[4 * j + 2],
-                     pk[4 * j + 3]);
+          for (int i = 0; i < 32; ++i) pk[i] = __float_as_uint(f[h * 32 + i]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) pk[i] = Elem<T>::pack2(f[2 * i], f[2 * i + 1]);
+        }
+        const uint32_t buf = cbuf + (nstore & 1) * L::kCBuf;
+        if (nstore >= 2 && lane == 0) bulk_wait_read<1>();
+        __syncwarp();
+        // Row `lane` of the box, 16-byte chunk j stored at j ^ (row % 8).
+        const uint32_t row = buf + lane * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          st_shared_v4(row + ((j ^ (lane & 7)) << 4), pk[4 * j], pk[4 * j + 1], pk[4 * j + 2],
+                       pk[4 * j + 3]);
+        }
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          // C is written once and not re-read here: evict it first so the A
+          // and B tiles other CTAs still need stay in L2.
+          tma_store_2d_hint(&tmC, buf, x + h * kBoxCols, y, c_policy);
+          bulk_commit();
+        }
+        ++nstore;
       }
-      fence_proxy_async_shared();
-      __syncwarp();
-      if (lane == 0) {
-        // C is written once and not re-read here: evict it first so the A
-        // and B tiles other CTAs still need stay in L2.
-        tma_store_2d_hint(&tmC, buf, x, y, c_policy);
-        bulk_commit();
-      }
-      ++nstore;
     };
     WorkItem w;
     for (int i = 0; work_item(sched, i, w); ++i) {
@@ -441,6 +537,11 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
         tmem_ld_32x32b_x32(trow + c * 64, r);
         tmem_ld_32x32b_x32(trow + c * 64 + 32, r + 32);
         tmem_wait_ld();
+        if constexpr (Op::kIntAcc) {
+          // s32 accumulator -> fp32 (exact below 2^24 in magnitude).
+#pragma unroll
+          for (int j = 0; j < 64; ++j) r[j] = __float_as_uint(static_cast<float>(static_cast<int>(r[j])));
+        }
         if (c == BN / 64 - 1) {
           // Accumulator fully read: hand it back to the MMA warp.
           tc_fence_before();
@@ -463,6 +564,18 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
         float f[64];
 #pragma unroll
         for (int j = 0; j < 64; ++j) f[j] = __uint_as_float(r[j]);
+        if constexpr (kScaled) {
+          const int row = mb * kBM + row_in_tile;
+          const float sa = row < M ? __ldg(sc.sa + static_cast<size_t>(row) * sc.sa_step) : 0.f;
+#pragma unroll
+          for (int j = 0; j < 64; j += 4) {
+            const float4 sb = load_sb4(sc, store_x + j, N);
+            f[j] = (f[j] * sa) * sb.x;
+            f[j + 1] = (f[j + 1] * sa) * sb.y;
+            f[j + 2] = (f[j + 2] * sa) * sb.z;
+            f[j + 3] = (f[j + 3] * sa) * sb.w;
+          }
+        }
         store_chunk(f, store_x, store_y);
       }
       if constexpr (kFused) {
@@ -541,10 +654,16 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
                   sum[u].w = silu_f(sum[u].w) * sum_up[u].w;
                 }
                 if (gr < M && gc < n_out) {  // n_out % 8 == 0: gc < n_out implies gc + 3 < n_out
-                  uint2 o;
-                  o.x = Elem<T>::pack2(sum[u].x, sum[u].y);
-                  o.y = Elem<T>::pack2(sum[u].z, sum[u].w);
-                  *reinterpret_cast<uint2*>(C + static_cast<size_t>(gr) * n_out + gc) = o;
+                  if constexpr (kScaled) {
+                    const float sa = __ldg(sc.sa + static_cast<size_t>(gr) * sc.sa_step);
+                    const float4 sb = load_sb4(sc, gc, N);
+                    sum[u].x = (sum[u].x * sa) * sb.x;
+                    sum[u].y = (sum[u].y * sa) * sb.y;
+                    sum[u].z = (sum[u].z * sa) * sb.z;
+                    sum[u].w = (sum[u].w * sa) * sb.w;
+                  }
+                  store4(C + static_cast<size_t>(gr) * n_out + gc, sum[u].x, sum[u].y, sum[u].z,
+                         sum[u].w);
                 }
               }
             }
@@ -651,13 +770,14 @@ struct TcPlan {
 // `rem` tiles - those tiles cut into S = min(4, sms / rem, kblocks / 4) K
 // splits, so the split units form one round over the SMs and the last wave
 // lasts about 1/S of a tile plus the partial-sum pass.
-TcPlan plan_tc(int M, int N, int K, int BN, int sms, bool allow_split) {
+// `bk` is the K block of the operand kind (64 16-bit or 128 8-bit elements).
+TcPlan plan_tc(int M, int N, int K, int BN, int bk, int sms, bool allow_split) {
   TcPlan p{};
   TcSched& s = p.sched;
   s.tiles_m = (M + kBM - 1) / kBM;
   s.tiles_n = (N + BN - 1) / BN;
   s.num_tiles = s.tiles_m * s.tiles_n;
-  s.kblocks = (K + kBK - 1) / kBK;
+  s.kblocks = (K + bk - 1) / bk;
   const int full = s.num_tiles / sms;
   const int rem = s.num_tiles - full * sms;
   int S = 1;
@@ -687,17 +807,30 @@ TcPlan plan_tc(int M, int N, int K, int BN, int sms, bool allow_split) {
   return p;
 }
 
-template <typename T, int BN, int STAGES, int kEpi = kEpiStore>
-int launch_tc(void* c, const void* a, const void* b, int M, int N, int K, bool bf16,
-              void* workspace, size_t ws_bytes, cudaStream_t stream, const DeviceInfo& info,
-              const ArParams* ar = nullptr) {
-  using L = TcLayout<BN, STAGES>;
+// Tensor map over a row-major matrix of T (16-bit or fp32).
+template <typename T>
+int make_tmap_of(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_cols,
+                 uint32_t box_rows) {
+  if constexpr (std::is_same<T, float>::value)
+    return make_tmap_2d_f32(map, base, rows, cols, cols, box_cols, box_rows);
+  else
+    return make_tmap_2d_16bit(map, base, std::is_same<T, __nv_bfloat16>::value, rows, cols, cols,
+                              box_cols, box_rows);
+}
+
+// Launches the persistent kernel on operands of kind Op (Op16<T> for the
+// 16-bit GEMMs, OpE4m3 / OpE5m2 / OpS8 for the scaled GEMM) with output type T.
+template <typename Op, typename T, int BN, int STAGES, int kEpi = kEpiStore>
+int launch_tc(void* c, const void* a, const void* b, int M, int N, int K, void* workspace,
+              size_t ws_bytes, cudaStream_t stream, const DeviceInfo& info,
+              const ArParams* ar = nullptr, const ScaleParams* scales = nullptr) {
+  using L = TcLayout<BN, STAGES, Op::kBytes>;
   constexpr bool kFused = kEpi == kEpiAllReduce;
-  auto kernel = gemm_tc_kernel<T, BN, STAGES, kEpi>;
+  auto kernel = gemm_tc_kernel<Op, T, BN, STAGES, kEpi>;
   if (int st = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), L::kAlloc, info)) return st;
-  TcPlan p = plan_tc(M, N, K, BN, info.sm_count, workspace != nullptr);
+  TcPlan p = plan_tc(M, N, K, BN, L::kBK, info.sm_count, workspace != nullptr);
   if (p.ws_bytes > 0 && (ws_bytes < p.ws_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255)))
-    p = plan_tc(M, N, K, BN, info.sm_count, false);
+    p = plan_tc(M, N, K, BN, L::kBK, info.sm_count, false);
   if (p.ws_bytes > 0) {
     p.sched.counters = static_cast<unsigned*>(workspace);
     p.sched.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + p.counter_bytes);
@@ -706,15 +839,22 @@ int launch_tc(void* c, const void* a, const void* b, int M, int N, int K, bool b
       return fail(AOTK_ERR_CUDA, "tcgen05 gemm: counter reset: %s", cudaGetErrorString(e));
   }
   CUtensorMap ta, tb, tc;
-  if (int st = make_tmap_2d_16bit(&ta, a, bf16, M, K, K, kBK, kBM)) return st;
-  if (int st = make_tmap_2d_16bit(&tb, b, bf16, K, N, N, 64, kBK)) return st;
+  if constexpr (Op::kBytes == 1) {
+    if (int st = make_tmap_2d_8bit(&ta, a, M, K, K, L::kBK, kBM)) return st;
+    if (int st = make_tmap_2d_8bit(&tb, b, K, N, N, L::kBoxN, L::kBK)) return st;
+  } else {
+    if (int st = make_tmap_of<T>(&ta, a, M, K, L::kBK, kBM)) return st;
+    if (int st = make_tmap_of<T>(&tb, b, K, N, L::kBoxN, L::kBK)) return st;
+  }
   const int n_out = kEpi == kEpiSiluMul ? N / 2 : N;
-  if (int st = make_tmap_2d_16bit(&tc, c, bf16, M, n_out, n_out, 64, 32)) return st;
-  const uint32_t idesc = idesc_f16(bf16, kBM, BN, /*a_mn_major=*/false, /*b_mn_major=*/true);
+  if (int st = make_tmap_of<T>(&tc, c, M, n_out, 128 / sizeof(T), 32)) return st;
+  const uint32_t idesc = Op::idesc(kBM, BN);  // A K-major, B MN-major
   ArParams arp{};
   if (ar) arp = *ar;
+  ScaleParams scp{};
+  if (scales) scp = *scales;
   kernel<<<p.grid, kFused ? kThreadsFused : kThreads, L::kAlloc, stream>>>(
-      ta, tb, tc, static_cast<T*>(c), M, N, K, idesc, p.sched, arp);
+      ta, tb, tc, static_cast<T*>(c), M, N, K, idesc, p.sched, arp, scp);
   return check_launch("tcgen05 gemm");
 }
 
@@ -726,7 +866,7 @@ constexpr int kTcStages = 4;
 size_t gemm_tc_workspace_size(int64_t M, int64_t N, int64_t K, int sm_count) {
   if (M <= 0 || N <= 0 || K <= 0 || M >= (1LL << 31) || N >= (1LL << 31) || K >= (1LL << 31))
     return 0;
-  return plan_tc((int)M, (int)N, (int)K, kTcBN, sm_count, true).ws_bytes;
+  return plan_tc((int)M, (int)N, (int)K, kTcBN, OpShape<2>::kBK, sm_count, true).ws_bytes;
 }
 
 int gemm_tc(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K, int dtype,
@@ -738,10 +878,10 @@ int gemm_tc(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int m = (int)M, n = (int)N, k = (int)K;
   if (dtype == AOTK_BFLOAT16)
-    return launch_tc<__nv_bfloat16, kTcBN, kTcStages, kEpiStore>(c, a, b, m, n, k, true, workspace,
-                                                                 ws_bytes, s, info);
-  return launch_tc<__half, kTcBN, kTcStages, kEpiStore>(c, a, b, m, n, k, false, workspace,
-                                                        ws_bytes, s, info);
+    return launch_tc<Op16<__nv_bfloat16>, __nv_bfloat16, kTcBN, kTcStages, kEpiStore>(
+        c, a, b, m, n, k, workspace, ws_bytes, s, info);
+  return launch_tc<Op16<__half>, __half, kTcBN, kTcStages, kEpiStore>(c, a, b, m, n, k, workspace,
+                                                                      ws_bytes, s, info);
 }
 
 int gemm_silu_mul(void* act, const void* a, const void* b, int64_t M, int64_t N2, int64_t K,
@@ -757,10 +897,51 @@ int gemm_silu_mul(void* act, const void* a, const void* b, int64_t M, int64_t N2
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int m = (int)M, n = (int)N2, k = (int)K;
   if (dtype == AOTK_BFLOAT16)
-    return launch_tc<__nv_bfloat16, kTcBN, kTcStages, kEpiSiluMul>(act, a, b, m, n, k, true,
-                                                                   workspace, ws_bytes, s, info);
-  return launch_tc<__half, kTcBN, kTcStages, kEpiSiluMul>(act, a, b, m, n, k, false, workspace,
-                                                          ws_bytes, s, info);
+    return launch_tc<Op16<__nv_bfloat16>, __nv_bfloat16, kTcBN, kTcStages, kEpiSiluMul>(
+        act, a, b, m, n, k, workspace, ws_bytes, s, info);
+  return launch_tc<Op16<__half>, __half, kTcBN, kTcStages, kEpiSiluMul>(act, a, b, m, n, k,
+                                                                        workspace, ws_bytes, s, info);
+}
+
+size_t gemm_scaled_tc_workspace_size(int64_t M, int64_t N, int64_t K, int sm_count) {
+  if (M <= 0 || N <= 0 || K <= 0 || M >= (1LL << 31) || N >= (1LL << 31) || K >= (1LL << 31))
+    return 0;
+  return plan_tc((int)M, (int)N, (int)K, kTcBN, OpShape<1>::kBK, sm_count, true).ws_bytes;
+}
+
+namespace {
+
+template <typename Op>
+int launch_scaled(void* c, const void* a, const void* b, int m, int n, int k, int out_dtype,
+                  const ScaleParams& sc, void* workspace, size_t ws_bytes, cudaStream_t s,
+                  const DeviceInfo& info) {
+  if (out_dtype == AOTK_BFLOAT16)
+    return launch_tc<Op, __nv_bfloat16, kTcBN, kTcStages, kEpiScaled>(c, a, b, m, n, k, workspace,
+                                                                      ws_bytes, s, info, nullptr, &sc);
+  if (out_dtype == AOTK_FLOAT16)
+    return launch_tc<Op, __half, kTcBN, kTcStages, kEpiScaled>(c, a, b, m, n, k, workspace,
+                                                               ws_bytes, s, info, nullptr, &sc);
+  return launch_tc<Op, float, kTcBN, kTcStages, kEpiScaled>(c, a, b, m, n, k, workspace, ws_bytes,
+                                                            s, info, nullptr, &sc);
+}
+
+}  // namespace
+
+int gemm_scaled_tc(void* c, const void* a, const void* b, const float* scale_a,
+                   const float* scale_b, int64_t M, int64_t N, int64_t K, int in_dtype,
+                   int out_dtype, int scale_mode, void* workspace, size_t ws_bytes, void* stream) {
+  DeviceInfo info;
+  if (int st = current_device_info(&info)) return st;
+  if (int st = require_sm100(info)) return st;
+  ScaleParams sc{scale_a, scale_b, scale_mode == AOTK_SCALE_ROW ? 1 : 0,
+                 scale_mode == AOTK_SCALE_ROW ? 1 : 0};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int m = (int)M, n = (int)N, k = (int)K;
+  if (in_dtype == AOTK_FLOAT8_E4M3)
+    return launch_scaled<OpE4m3>(c, a, b, m, n, k, out_dtype, sc, workspace, ws_bytes, s, info);
+  if (in_dtype == AOTK_FLOAT8_E5M2)
+    return launch_scaled<OpE5m2>(c, a, b, m, n, k, out_dtype, sc, workspace, ws_bytes, s, info);
+  return launch_scaled<OpS8>(c, a, b, m, n, k, out_dtype, sc, workspace, ws_bytes, s, info);
 }
 
 int gemm_allreduce_tiles(int64_t M, int64_t N) {
@@ -796,10 +977,10 @@ int gemm_allreduce(const void* a, const void* b, int64_t M, int64_t N, int64_t K
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int m = (int)M, n = (int)N, k = (int)K;
   if (dtype == AOTK_BFLOAT16)
-    return launch_tc<__nv_bfloat16, kTcBN, kTcStages, kEpiAllReduce>(bufs->part, a, b, m, n, k,
-                                                                     true, nullptr, 0, s, info, &ar);
-  return launch_tc<__half, kTcBN, kTcStages, kEpiAllReduce>(bufs->part, a, b, m, n, k, false,
-                                                            nullptr, 0, s, info, &ar);
+    return launch_tc<Op16<__nv_bfloat16>, __nv_bfloat16, kTcBN, kTcStages, kEpiAllReduce>(
+        bufs->part, a, b, m, n, k, nullptr, 0, s, info, &ar);
+  return launch_tc<Op16<__half>, __half, kTcBN, kTcStages, kEpiAllReduce>(
+      bufs->part, a, b, m, n, k, nullptr, 0, s, info, &ar);
 }
 
 int watchdog_selftest(void* stream) {

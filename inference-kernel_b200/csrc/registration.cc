@@ -1,5 +1,7 @@
 // torch operator library `aot_kernel`: the same schemas as the reference's
-// registration (aot_kernel/csrc/registration.cc:10-25) plus silu_mul_forward.
+// registration (aot_kernel/csrc/registration.cc:10-25) plus the fused ops
+// (silu_mul_forward, add_rmsnorm_forward, gemm_silu_mul) and scaled_gemm, the
+// 8-bit GEMM the reference provides as a Triton kernel.
 // Each kernel checks its tensors, pins the device, and calls the C ABI of
 // libaotk (include/aotk.h) on the current torch stream.  Unlike the
 // reference, launches go to at::cuda::getCurrentCUDAStream() under a device
@@ -229,6 +231,70 @@ void gemm_silu_mul(at::Tensor out, at::Tensor a, at::Tensor b_gate_up) {
                op);
 }
 
+// out = (a @ b) * scale_a * scale_b for 8-bit a / b (e4m3, e5m2 or int8);
+// scale_a / scale_b fp32 with 1 value each or M / N values.  `optimized`
+// selects the tensor-core dispatch (tcgen05 where the shape allows) or the
+// SIMT kernel, as the reference's flag selects its optimized or naive kernel.
+void scaled_gemm(at::Tensor out, at::Tensor a, at::Tensor b, at::Tensor scale_a,
+                 at::Tensor scale_b, bool optimized) {
+  const char* op = "scaled_gemm";
+  check_cuda(a, op, "a");
+  check_cuda(b, op, "b");
+  check_cuda(out, op, "out");
+  check_cuda(scale_a, op, "scale_a");
+  check_cuda(scale_b, op, "scale_b");
+  check_same(a, b, op, "a", "b");
+  TORCH_CHECK(out.device() == a.device() && scale_a.device() == a.device() &&
+                  scale_b.device() == a.device(),
+              "[", op, "] tensors are not on one device");
+  int in_dtype = -1;
+  switch (a.scalar_type()) {
+    case at::ScalarType::Float8_e4m3fn: in_dtype = AOTK_FLOAT8_E4M3; break;
+    case at::ScalarType::Float8_e5m2: in_dtype = AOTK_FLOAT8_E5M2; break;
+    case at::ScalarType::Char: in_dtype = AOTK_INT8; break;
+    default: TORCH_CHECK(false, "[", op, "] unsupported input dtype: ", a.scalar_type());
+  }
+  const int out_dtype = aotk_dtype(out, op);
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "[", op, "] expects 2D tensors");
+  TORCH_CHECK(a.size(1) == b.size(0), "[", op, "] inner dims mismatch: ", a.size(1), " vs ",
+              b.size(0));
+  const int64_t M = a.size(0), K = a.size(1), N = b.size(1);
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "[", op, "] out must be [", M, ", ", N,
+              "], got ", out.sizes());
+  TORCH_CHECK(a.is_contiguous() && b.is_contiguous() && out.is_contiguous(), "[", op,
+              "] tensors must be contiguous");
+  TORCH_CHECK(scale_a.scalar_type() == at::kFloat && scale_b.scalar_type() == at::kFloat, "[", op,
+              "] scales must be float32");
+  TORCH_CHECK(scale_a.is_contiguous() && scale_b.is_contiguous(), "[", op,
+              "] scales must be contiguous");
+  int mode = -1;
+  if (scale_a.numel() == 1 && scale_b.numel() == 1)
+    mode = AOTK_SCALE_TENSOR;
+  else if (scale_a.numel() == M && scale_b.numel() == N)
+    mode = AOTK_SCALE_ROW;
+  TORCH_CHECK(mode >= 0, "[", op, "] expect tensorwise (scalar scale_a and scale_b) or rowwise ",
+              "(scale_a.numel()==M, scale_b.numel()==N), got ", scale_a.numel(), " and ",
+              scale_b.numel());
+  c10::cuda::CUDAGuard guard(a.device());
+  const auto* sa = static_cast<const float*>(scale_a.data_ptr());
+  const auto* sb = static_cast<const float*>(scale_b.data_ptr());
+  if (!optimized) {
+    check_status(aotk_scaled_gemm_simt(out.data_ptr(), a.data_ptr(), b.data_ptr(), sa, sb, M, N,
+                                       K, in_dtype, out_dtype, mode, current_stream(a)),
+                 op);
+    return;
+  }
+  size_t ws_bytes = 0;
+  check_status(aotk_scaled_gemm_workspace_size(M, N, K, in_dtype, &ws_bytes), op);
+  at::Tensor ws;
+  if (ws_bytes > 0)
+    ws = at::empty({static_cast<int64_t>(ws_bytes)}, a.options().dtype(at::kByte));
+  check_status(aotk_scaled_gemm(out.data_ptr(), a.data_ptr(), b.data_ptr(), sa, sb, M, N, K,
+                                in_dtype, out_dtype, mode, ws_bytes > 0 ? ws.data_ptr() : nullptr,
+                                ws_bytes, current_stream(a)),
+               op);
+}
+
 }  // namespace
 
 TORCH_LIBRARY(aot_kernel, m) {
@@ -257,6 +323,11 @@ TORCH_LIBRARY(aot_kernel, m) {
 
   m.def("gemm_silu_mul(Tensor! out, Tensor a, Tensor b_gate_up) -> ()");
   m.impl("gemm_silu_mul", c10::kCUDA, &gemm_silu_mul);
+
+  m.def(
+      "scaled_gemm(Tensor! out, Tensor a, Tensor b, Tensor scale_a, Tensor scale_b, bool "
+      "optimized) -> ()");
+  m.impl("scaled_gemm", c10::kCUDA, &scaled_gemm);
 }
 
 // `import aot_kernel._C` runs the static registration above; the module itself is empty.

@@ -187,6 +187,28 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint6
       : "memory");
 }
 
+// D[tmem] (+)= A * B, kind::f8f6f4 (here e4m3 or e5m2 in, fp32 acc).
+__device__ __forceinline__ void umma_f8f6f4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      : "memory");
+}
+
+// D[tmem] (+)= A * B, kind::i8 (signed 8-bit in, s32 acc).
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                        uint32_t idesc, bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      : "memory");
+}
+
 // Arrives once on `bar` when every tcgen05.mma issued so far by this thread
 // has completed.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
@@ -315,6 +337,16 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int m, int n, bool a
   return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
          ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
          (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// Instruction descriptor for any dense kind: D format `c_fmt` (1 = f32,
+// 2 = s32), A / B formats `ab_fmt` (kind::f8f6f4: 0 = e4m3, 1 = e5m2;
+// kind::i8: 1 = signed), majors and shape as in idesc_f16.
+__host__ __device__ constexpr uint32_t idesc_make(uint32_t c_fmt, uint32_t ab_fmt, int m, int n,
+                                                  bool a_mn_major, bool b_mn_major) {
+  return (c_fmt << 4) | (ab_fmt << 7) | (ab_fmt << 10) | ((a_mn_major ? 1u : 0u) << 15) |
+         ((b_mn_major ? 1u : 0u) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
 }
 
 // ---- programmatic dependent launch ---------------------------------------------

@@ -33,18 +33,15 @@ int encoder(EncodeTiledFn* fn) {
   return AOTK_OK;
 }
 
-}  // namespace
-
-int make_tmap_2d_16bit(CUtensorMap* map, const void* base, bool bf16, uint64_t rows, uint64_t cols,
-                       uint64_t ld, uint32_t box_cols, uint32_t box_rows) {
+int encode_2d(CUtensorMap* map, CUtensorMapDataType type, uint32_t elem_bytes, const void* base,
+              uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols, uint32_t box_rows) {
   EncodeTiledFn fn;
   if (int st = encoder(&fn)) return st;
   const cuuint64_t dims[2] = {cols, rows};
-  const cuuint64_t strides[1] = {ld * 2};
+  const cuuint64_t strides[1] = {ld * elem_bytes};
   const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estrides[2] = {1, 1};
-  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                  const_cast<void*>(base), dims, strides, box, estrides,
+  CUresult r = fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estrides,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -54,6 +51,24 @@ int make_tmap_2d_16bit(CUtensorMap* map, const void* base, bool bf16, uint64_t r
                 box_cols, box_rows);
   }
   return AOTK_OK;
+}
+
+}  // namespace
+
+int make_tmap_2d_8bit(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                      uint32_t box_cols, uint32_t box_rows) {
+  return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, base, rows, cols, ld, box_cols, box_rows);
+}
+
+int make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                     uint32_t box_cols, uint32_t box_rows) {
+  return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, rows, cols, ld, box_cols, box_rows);
+}
+
+int make_tmap_2d_16bit(CUtensorMap* map, const void* base, bool bf16, uint64_t rows, uint64_t cols,
+                       uint64_t ld, uint32_t box_cols, uint32_t box_rows) {
+  return encode_2d(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                   base, rows, cols, ld, box_cols, box_rows);
 }
 
 }  // namespace aotk

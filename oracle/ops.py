@@ -155,3 +155,104 @@ def mlp_block_sharded(x, norm_w, w_gate_up, w_down, eps: float, dtype: str, worl
         part = gemm(act, w_down[cols, :], dtype)
         total = part if total is None else total + part
     return round_to(total, dtype)
+
+
+# ---- 8-bit formats and the scaled GEMM ----------------------------------------
+
+QDTYPES = ("e4m3", "e5m2", "int8")
+
+# (exponent bits, mantissa bits, bias) of the OCP 8-bit float formats torch
+# names float8_e4m3fn and float8_e5m2.
+_FP8_FORMATS = {"e4m3": (4, 3, 7), "e5m2": (5, 2, 15)}
+
+
+def _fp8_positive_values(kind: str) -> np.ndarray:
+    """Values of the codes 0..127 (sign bit clear) as float64; NaN / inf where
+    the format has them (e4m3fn: 0x7F is NaN, no infinities; e5m2: exponent
+    all ones is inf (mantissa 0) or NaN)."""
+    e_bits, m_bits, bias = _FP8_FORMATS[kind]
+    codes = np.arange(128)
+    e = codes >> m_bits
+    m = codes & ((1 << m_bits) - 1)
+    frac = m / float(1 << m_bits)
+    v = np.where(e == 0, frac * 2.0 ** (1 - bias), (1.0 + frac) * 2.0 ** (e - bias))
+    if kind == "e4m3":
+        v[127] = np.nan
+    else:
+        top = (1 << e_bits) - 1
+        v[(e == top) & (m == 0)] = np.inf
+        v[(e == top) & (m != 0)] = np.nan
+    return v
+
+
+def fp8_decode(codes: np.ndarray, kind: str) -> np.ndarray:
+    """uint8 codes -> float32 values (exact: every fp8 value is a float32)."""
+    c = np.asarray(codes, dtype=np.uint8)
+    pos = _fp8_positive_values(kind)[c & 0x7F]
+    return np.where(c & 0x80, -pos, pos).astype(np.float32)
+
+
+def fp8_encode(x: np.ndarray, kind: str) -> np.ndarray:
+    """float32 -> uint8 codes, round to nearest, ties to the even code, the
+    sign kept for zeros.  Magnitudes that round past the largest finite value
+    become NaN (e4m3fn, which has no infinity) or inf (e5m2); NaN stays NaN.
+    Restates torch's ``Tensor.to(torch.float8_e4m3fn / float8_e5m2)`` on CPU,
+    the conversion the reference's tests quantise with
+    (tests/gemm/test_triton.py:85-93)."""
+    x = np.asarray(x, dtype=np.float32)
+    vals = _fp8_positive_values(kind)
+    n_finite = 127 if kind == "e4m3" else 124  # codes 0 .. n_finite-1 are finite
+    over_code = 127 if kind == "e4m3" else 124  # NaN resp. +inf
+    # Finite values plus the value the format would have next, so that
+    # rounding just past the maximum behaves as in an unbounded format.
+    top = vals[n_finite - 1]
+    step = top - vals[n_finite - 2]
+    table = np.append(vals[:n_finite], top + step)
+    mag = np.abs(x.astype(np.float64))
+    hi = np.clip(np.searchsorted(table, mag, side="left"), 1, len(table) - 1)
+    lo = hi - 1
+    d_lo = mag - table[lo]
+    d_hi = table[hi] - mag
+    pick_hi = (d_hi < d_lo) | ((d_hi == d_lo) & (hi % 2 == 0))
+    code = np.where(pick_hi, hi, lo)
+    code = np.where(mag > table[-1], n_finite, code)   # beyond the virtual value
+    code = np.where(code >= n_finite, over_code, code)
+    code = np.where(np.isnan(x), 127, code)
+    sign = np.signbit(x) & ~np.isnan(x)
+    return (code | np.where(sign, 0x80, 0)).astype(np.uint8)
+
+
+def dequant(q: np.ndarray, qdtype: str) -> np.ndarray:
+    """8-bit inputs -> float64 values: fp8 codes decoded, int8 as integers."""
+    if qdtype == "int8":
+        return np.asarray(q).view(np.int8).astype(np.float64)
+    return fp8_decode(q, qdtype).astype(np.float64)
+
+
+def scaled_gemm(a_q: np.ndarray, b_q: np.ndarray, scale_a: np.ndarray, scale_b: np.ndarray,
+                qdtype: str, out_dtype: str) -> np.ndarray:
+    """The reference's ``scaled_gemm`` (jit_kernel/gemm.py:199-248; kernels
+    jit_kernel/gemm.py:86-123 and 144-196): acc = A @ B accumulated in fp32
+    (restated in float64, which is exact for int8 and holds the fp8 sum to
+    far below fp32 rounding), then ``acc * scale_a[m] * scale_b[n]`` in fp32,
+    left to right, and one rounding to the output dtype.  scale_a / scale_b
+    hold one value each (tensorwise) or M / N values (rowwise)."""
+    a = dequant(a_q, qdtype)
+    b = dequant(b_q, qdtype)
+    acc = (a @ b).astype(np.float32)
+    sa = np.asarray(scale_a, dtype=np.float32).reshape(-1)
+    sb = np.asarray(scale_b, dtype=np.float32).reshape(-1)
+    sa = sa.reshape(-1, 1) if sa.size == acc.shape[0] and sa.size != 1 else sa.reshape(1, 1)
+    sb = sb.reshape(1, -1) if sb.size == acc.shape[1] and sb.size != 1 else sb.reshape(1, 1)
+    y = (acc * sa) * sb
+    return round_to(y.astype(np.float32), out_dtype)
+
+
+def scaled_gemm_dequant_first(a_q, b_q, scale_a, scale_b, qdtype: str, out_dtype: str):
+    """The reference tests' formulation (tests/gemm/test_triton.py:104-107):
+    ``(a.float() * scale_a[:, None]) @ (b.float() * scale_b[None, :])`` in
+    fp32, rounded once.  Differs from ``scaled_gemm`` only by fp32 rounding
+    before the final rounding."""
+    a = dequant(a_q, qdtype).astype(np.float32) * np.asarray(scale_a, np.float32).reshape(-1, 1)
+    b = dequant(b_q, qdtype).astype(np.float32) * np.asarray(scale_b, np.float32).reshape(1, -1)
+    return round_to((a.astype(np.float64) @ b.astype(np.float64)).astype(np.float32), out_dtype)

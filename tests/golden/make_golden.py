@@ -44,6 +44,8 @@ def digest(a: np.ndarray) -> str:
 def run_reference(ref, case, inputs):
     import torch
 
+    if case.op == "scaled_gemm":
+        return run_reference_scaled(case, inputs)
     tdt = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16}[case.dtype]
     t = [torch.from_numpy(np.ascontiguousarray(x)).to(tdt) for x in inputs]
     if case.op == "gemm":
@@ -61,6 +63,29 @@ def run_reference(ref, case, inputs):
     else:
         raise ValueError(case.op)
     return y.float().numpy()
+
+
+def run_reference_scaled(case, inputs):
+    """The reference's scaled-GEMM oracle, ``_scaled_reference`` of
+    tests/gemm/test_triton.py:104-107, on CPU tensors of the case's inputs."""
+    import importlib
+
+    import torch
+
+    mod = importlib.import_module("tests.gemm.test_triton")  # the reference's test module
+    qt = {"e4m3": torch.float8_e4m3fn, "e5m2": torch.float8_e5m2, "int8": torch.int8}[case.qdtype]
+    a_q, b_q, sa, sb = inputs
+    a = torch.from_numpy(np.ascontiguousarray(a_q)).view(qt)
+    b = torch.from_numpy(np.ascontiguousarray(b_q)).view(qt)
+    out_dt = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16}[case.dtype]
+    y = mod._scaled_reference(a, b, torch.from_numpy(sa), torch.from_numpy(sb), out_dt)
+    return y.float().numpy()
+
+
+def input_digest(x: np.ndarray, case) -> str:
+    if x.dtype in (np.uint8, np.int8) or case.op == "scaled_gemm":
+        return digest(x)
+    return digest(bits(x, case.dtype))
 
 
 def main() -> None:
@@ -89,7 +114,7 @@ def main() -> None:
             "dtype": case.dtype,
             "eps": case.eps,
             "sample_rows": case.sample_rows,
-            "input_sha256": [digest(bits(x, case.dtype)) for x in inputs],
+            "input_sha256": [input_digest(x, case) for x in inputs],
             "output_sha256": digest(b),
         }
         print(f"{case.id}: {out.shape}")

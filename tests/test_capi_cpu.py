@@ -51,6 +51,19 @@ def test_version():
         (lambda: capi.relu_forward(None, None, 8, 2), capi.ERR_INVALID_ARGUMENT),
         (lambda: capi.rmsnorm_forward(0, 0, 0, -1, 8, 1e-6, 2), capi.ERR_INVALID_ARGUMENT),
         (lambda: capi.silu_mul_forward(8, 4, 8, 4, 8, 4, 2, 8, 2), capi.ERR_INVALID_ARGUMENT),  # stride < cols
+        # scaled GEMM: 16-bit input, bad output dtype, bad scale mode, null scale, negative size
+        (lambda: capi.scaled_gemm(16, 16, 16, 16, 16, 4, 4, 4, capi.BFLOAT16, capi.BFLOAT16,
+                                  capi.SCALE_TENSOR), capi.ERR_UNSUPPORTED),
+        (lambda: capi.scaled_gemm(16, 16, 16, 16, 16, 4, 4, 4, capi.INT8, capi.INT8,
+                                  capi.SCALE_TENSOR), capi.ERR_UNSUPPORTED),
+        (lambda: capi.scaled_gemm(16, 16, 16, 16, 16, 4, 4, 4, capi.FLOAT8_E4M3, capi.BFLOAT16,
+                                  7), capi.ERR_INVALID_ARGUMENT),
+        (lambda: capi.scaled_gemm(16, 16, 16, None, 16, 4, 4, 4, capi.FLOAT8_E4M3, capi.BFLOAT16,
+                                  capi.SCALE_ROW), capi.ERR_INVALID_ARGUMENT),
+        (lambda: capi.scaled_gemm_simt(16, 16, 16, 16, 16, 4, -4, 4, capi.INT8, capi.FLOAT32,
+                                       capi.SCALE_ROW), capi.ERR_INVALID_ARGUMENT),
+        (lambda: capi.scaled_gemm_tc(16, 16, 16, 16, 16, 4, 4, 0, capi.FLOAT8_E5M2, capi.FLOAT16,
+                                     capi.SCALE_ROW), capi.ERR_INVALID_ARGUMENT),  # empty K
     ],
 )
 def test_argument_errors_without_device(call, status):
@@ -65,6 +78,8 @@ def test_empty_problems_are_no_ops():
     capi.silu_forward(0, 0, 0, capi.BFLOAT16)
     capi.rmsnorm_forward(0, 0, 0, 0, 4096, 1e-6, capi.BFLOAT16)
     capi.silu_mul_forward(0, 0, 0, 0, 0, 0, 0, 16, capi.BFLOAT16)
+    capi.scaled_gemm(0, 0, 0, 0, 0, 0, 16, 16, capi.INT8, capi.BFLOAT16, capi.SCALE_TENSOR)
+    assert capi.scaled_gemm_workspace_size(256, 250, 256, capi.FLOAT8_E4M3) == 0  # N % 16 != 0
 
 
 def test_torch_extension_registers_reference_schemas():
@@ -74,8 +89,10 @@ def test_torch_extension_registers_reference_schemas():
 
     ops = torch.ops.aot_kernel
     for name in ("gemm", "gemm_opt", "rmsnorm_forward", "silu_forward", "relu_forward",
-                 "silu_mul_forward"):
+                 "silu_mul_forward", "add_rmsnorm_forward", "gemm_silu_mul", "scaled_gemm"):
         assert hasattr(ops, name)
+    schema = ops.scaled_gemm.default._schema
+    assert [a.name for a in schema.arguments] == ["out", "a", "b", "scale_a", "scale_b", "optimized"]
     schema = ops.rmsnorm_forward.default._schema
     assert [a.name for a in schema.arguments] == ["out", "x", "weight", "eps"]
     assert schema.arguments[0].alias_info.is_write and str(schema.arguments[3].type) == "float"

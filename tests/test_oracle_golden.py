@@ -3,7 +3,10 @@ package (tests/golden/make_golden.py).  CPU only.
 
 Pins: 16-bit outputs equal the reference bit for bit except for a few
 outputs one unit in the last place away (summation order of the GEMM, last-bit
-differences of exp); fp32 outputs within 1e-6 of max|ref|.
+differences of exp, where the scaled GEMM applies its scales); fp32 outputs
+within 1e-6 of max|ref|.  The scaled-GEMM goldens come from the reference
+tests' own oracle (tests/gemm/test_triton.py:104-107), and the fp8 codec is
+pinned to torch's float8 conversions.
 """
 
 from __future__ import annotations
@@ -63,7 +66,11 @@ def test_golden_covers_every_case(golden, manifest):
 
 @pytest.mark.parametrize("case", CASES, ids=lambda c: c.id)
 def test_inputs_regenerate_bit_exact(case, manifest):
-    digests = [hashlib.sha256(_bits(x, case.dtype).tobytes()).hexdigest() for x in make_inputs(case)]
+    def digest(x):
+        raw = np.ascontiguousarray(x) if case.op == "scaled_gemm" else _bits(x, case.dtype)
+        return hashlib.sha256(raw.tobytes()).hexdigest()
+
+    digests = [digest(x) for x in make_inputs(case)]
     assert digests == manifest["cases"][case.id]["input_sha256"]
 
 
@@ -84,8 +91,53 @@ def test_oracle_matches_reference(case, golden):
             a, b = make_inputs(case)
             mag = sampled(case, np.abs(a) @ np.abs(b))
             bound = bound + case.shape[1] * 2.0**-24 * mag
+        if case.op == "scaled_gemm":
+            # The reference scales the operands before an fp32 matmul, the
+            # oracle scales the accumulator: both round each scaled operand or
+            # product and the fp32 sum, K + 2 roundings of 2^-24 at most.
+            a_q, b_q, sa, sb = make_inputs(case)
+            a = np.abs(ops.dequant(a_q, case.qdtype)) * np.abs(sa.reshape(-1, 1))
+            b = np.abs(ops.dequant(b_q, case.qdtype)) * np.abs(sb.reshape(1, -1))
+            bound = bound + (case.shape[1] + 2) * 2.0**-24 * (a @ b)
         assert np.all(diff <= bound), "a 16-bit output is more than one ulp off"
-        assert np.mean(diff == 0) >= 0.999
+        assert np.mean(diff == 0) >= (0.99 if case.op == "scaled_gemm" else 0.999)
+
+
+@pytest.mark.parametrize("kind", ["e4m3", "e5m2"])
+def test_fp8_codec_matches_torch(kind):
+    """fp8_encode / fp8_decode against torch's CPU float8 conversions (the
+    conversion the reference's tests quantise with), over all 256 codes and
+    1.2M values spanning subnormals, rounding ties and overflow."""
+    torch = pytest.importorskip("torch")
+    tdt = {"e4m3": torch.float8_e4m3fn, "e5m2": torch.float8_e5m2}[kind]
+    codes = np.arange(256, dtype=np.uint8)
+    want = torch.from_numpy(codes).view(tdt).float().numpy()
+    assert np.array_equal(ops.fp8_decode(codes, kind), want, equal_nan=True)
+    rng = np.random.default_rng(7)
+    x = np.concatenate([rng.standard_normal(150_000).astype(np.float32) * np.float32(s)
+                        for s in (1e-4, 1e-2, 1.0, 10.0, 1e2, 1e3, 1e4, 1e5)])
+    # midpoints between neighbouring codes (ties) and the overflow edges
+    vals = ops.fp8_decode(codes[:127], kind).astype(np.float64)
+    vals = vals[np.isfinite(vals)]
+    mids = ((vals[1:] + vals[:-1]) / 2).astype(np.float32)
+    edges = np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 464, 465, 480, 59392, 59391, 61440],
+                     dtype=np.float32)
+    x = np.concatenate([x, mids, -mids, edges])
+    want = torch.from_numpy(x).to(tdt).view(torch.uint8).numpy()
+    assert np.array_equal(ops.fp8_encode(x, kind), want)
+
+
+def test_scaled_gemm_int8_is_exact():
+    """int8 products summed in float64 are exact; the scaled result equals an
+    integer matmul scaled in fp32."""
+    from oracle.inputs import quantized, scales
+
+    a = quantized((33, 70), 1, "int8")
+    b = quantized((70, 17), 2, "int8")
+    sa, sb = scales(33, 17, "row", 3)
+    acc = (a.astype(np.int64) @ b.astype(np.int64)).astype(np.float32)
+    want = ops.round_to((acc * sa.reshape(-1, 1)) * sb.reshape(1, -1), "float32")
+    assert np.array_equal(ops.scaled_gemm(a, b, sa, sb, "int8", "float32"), want)
 
 
 def test_special_values():

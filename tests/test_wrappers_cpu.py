@@ -37,3 +37,18 @@ def test_activation_rejects_cpu_tensor(fn):
 def test_silu_mul_rejects_cpu_tensor():
     with pytest.raises((ValueError, RuntimeError)):
         silu_mul(torch.randn(8), torch.randn(8))
+
+
+def test_scaled_gemm_checks_before_device_work():
+    """The reference's scaled_gemm checks (jit_kernel/gemm.py:207-226): 2-D
+    inputs (AssertionError), CUDA tensors (RuntimeError), matching K."""
+    from aot_kernel.gemm import scaled_gemm
+
+    a = torch.zeros(8, 16, dtype=torch.int8)
+    b = torch.zeros(16, 8, dtype=torch.int8)
+    s = torch.ones(1)
+    with pytest.raises(AssertionError):
+        scaled_gemm(torch.zeros(8, dtype=torch.int8), b, s, s)
+    with pytest.raises(RuntimeError):
+        scaled_gemm(a, b, s, s)
+    assert "scaled_gemm" in aot_kernel.__all__
