@@ -2,26 +2,32 @@
 //
 // One CTA per SM walks output tiles of 128 x BN (grouped raster for L2
 // reuse).  Six warps split the work:
-//   warp 0      TMA producer: per 64-wide K block, one 128 x 64 box of A
-//               (K-major) and BN/64 boxes of 64 x 64 of B (N-major), all
+//   warp 0      TMA producer: per K block (one 128-byte swizzle row of
+//               elements: 64 16-bit or 128 8-bit), one 128-row box of A
+//               (K-major) and BN / box-width boxes of B (N-major), all
 //               128-byte swizzled, into a STAGES-deep shared-memory ring
 //               guarded by full/empty mbarriers;
-//   warp 1      MMA issuer: allocates 2 * BN TMEM columns (two fp32
-//               accumulators), issues tcgen05.mma M=128 N=BN K=16 with A
-//               K-major and B MN-major straight from the swizzled stages (no
-//               transpose pass), and commits each stage back to the
-//               producer and each finished accumulator to the epilogue;
-//   warps 2-5   epilogue: tcgen05.ld of their 32-lane TMEM quarter, fp32 ->
-//               16-bit, swizzled 32 x 64 staging boxes, TMA stores (double
-//               buffered per warp).  The accumulator is handed back as soon
-//               as it is read, so the next tile's main loop overlaps this
-//               tile's stores.
-// Schedule: whole tiles are dealt round-robin to the CTAs; when the tile count
-// leaves a partial last wave, those last tiles are instead cut along K into S
-// units spread over all SMs.  A unit writes its fp32 partial tile to a
-// caller-provided workspace; the unit that finishes last (atomic counter per
-// tile) sums the S partials in split order and stores the 16-bit result, so
-// the output is deterministic.  Without a workspace the last wave runs whole.
+//   warp 1      MMA issuer: allocates 2 * BN TMEM columns (two 32-bit
+//               accumulators), issues tcgen05.mma M=128 N=BN (kind::f16 for
+//               fp16/bf16, K=16; kind::f8f6f4 / kind::i8 for the scaled
+//               8-bit GEMM, K=32) with A K-major and B MN-major straight from
+//               the swizzled stages (no transpose pass), and commits each
+//               stage back to the producer and each finished accumulator to
+//               the epilogue;
+//   warps 2-5   epilogue: tcgen05.ld of their 32-lane TMEM quarter, the
+//               variant's arithmetic (none, silu(gate) * up, dequantisation
+//               scales), packing to the output type, swizzled 32-row staging
+//               boxes and TMA stores (double buffered per warp).  The
+//               accumulator is handed back as soon as it is read, so the
+//               next tile's main loop overlaps this tile's stores.
+// Schedule: whole tiles are dealt round-robin to the CTAs.  A partial last
+// wave is cut to occupy more SMs (plan_tc): into two N halves per tile (an
+// MMA of N = BN/2 each; no workspace, results identical to whole tiles) or,
+// for a small remainder, long K and a caller-provided workspace, into S K
+// ranges whose fp32 partial tiles meet in the workspace: the unit that
+// arrives last (atomic counter per tile) waits for the others' partials,
+// adds them to its own accumulator in split order - so the output is
+// deterministic - and stores the result.
 // Every pipeline wait is bounded (sm100.cuh): on a timeout the kernel records
 // a watchdog bit, lets the other roles drop out, drains its in-flight copies
 // and frees TMEM before returning.
@@ -49,8 +55,19 @@ constexpr int kThreads = 192;       // plain GEMM: producer, MMA, 4 epilogue war
 constexpr int kThreadsFused = 320;  // + 4 all-reduce warps (gemm_allreduce)
 constexpr int kGroupM = 16;  // M tiles per raster group
 constexpr int kMaxSplits = 4;
+// K blocks below which a K split does not pay for its partial-tile traffic
+// (measured on B200: a 4-way split of 64 K blocks lost to whole tiles, of 128
+// K blocks it cut the kernel time by 13 %).
+constexpr int kSplitMinKblocks = 128;
 
-enum : unsigned { kWdProducer = 1u, kWdMma = 2u, kWdEpilogue = 4u, kWdPeer = 64u, kWdSelfTest = 128u };
+enum : unsigned {
+  kWdProducer = 1u,
+  kWdMma = 2u,
+  kWdEpilogue = 4u,
+  kWdSplit = 8u,  // the last K-split unit gave up waiting for the other partials
+  kWdPeer = 64u,
+  kWdSelfTest = 128u
+};
 
 __device__ unsigned g_never_set;  // stays 0: the self-test's flag that nothing sets
 
@@ -123,6 +140,8 @@ struct TcLayout {
   static constexpr uint32_t kTmemCols = 2 * BN;
   static_assert(BN % 64 == 0 && BN <= 256, "BN must be 64..256 in steps of 64");
   static_assert(kTmemCols <= 512, "two accumulators must fit in TMEM");
+  // The last K-split unit stages up to 4 partials x 16 x 128 x 16 bytes in the ring.
+  static_assert(4 * 16 * 128 * 16 <= STAGES * kStageBytes, "stage ring too small for partials");
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& mb, int& nb) {
@@ -135,20 +154,26 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
   nb = local / gm;
 }
 
-// Work list shared by the producer, MMA and epilogue roles of a CTA.
+// Work list shared by the producer, MMA and epilogue roles of a CTA.  Tiles
+// before split_begin run whole; the tail tiles from split_begin on run either
+// as two halves of 128 x BN/2 (halves != 0: twice the CTAs, no reduction) or
+// as `splits` K ranges whose fp32 partials meet in the workspace.
 struct TcSched {
   int tiles_m, tiles_n, num_tiles, kblocks;
   int full_rounds;    // rounds of whole tiles: tile = cta + r * grid, tile < split_begin
-  int split_begin;    // first tile computed in K splits (num_tiles when none)
-  int splits;         // units per split tile
+  int split_begin;    // first tail tile (num_tiles when none)
+  int halves;         // 1: tail tiles run as two N halves
+  int splits;         // K units per tail tile (1 with halves)
   int kb_per_split;
-  int units;          // (num_tiles - split_begin) * splits
-  float* ws;          // [units][kBM][BN] fp32 partial tiles
-  unsigned* counters; // [num_tiles - split_begin] arrivals per split tile
+  int units;          // tail work items: (num_tiles - split_begin) * (halves ? 2 : splits)
+  float* ws;          // [units][kBM][BN] fp32 partial tiles (K splits)
+  unsigned* counters; // [2][num_tiles - split_begin]: arrivals, then partials stored
 };
 
 struct WorkItem {
-  int tile, kb0, kb1, unit;  // unit < 0: whole tile
+  int tile, kb0, kb1;
+  int unit;  // >= 0: K-split unit (index into the workspace); -1 otherwise
+  int half;  // 0 / 1: N half of the tile; -1: the whole width
 };
 
 __device__ __forceinline__ bool work_item(const TcSched& s, int i, WorkItem& w) {
@@ -158,19 +183,66 @@ __device__ __forceinline__ bool work_item(const TcSched& s, int i, WorkItem& w) 
     w.kb0 = 0;
     w.kb1 = s.kblocks;
     w.unit = -1;
+    w.half = -1;
     return true;
   }
   const int u = blockIdx.x + (i - s.full_rounds) * gridDim.x;
   if (u >= s.units) return false;
+  if (s.halves) {
+    w.tile = s.split_begin + (u >> 1);
+    w.half = u & 1;
+    w.kb0 = 0;
+    w.kb1 = s.kblocks;
+    w.unit = -1;
+    return true;
+  }
   w.tile = s.split_begin + u / s.splits;
   w.kb0 = (u % s.splits) * s.kb_per_split;
   w.kb1 = min(s.kblocks, w.kb0 + s.kb_per_split);
   w.unit = u;
+  w.half = -1;
   return true;
+}
+
+// Global column of B box `j` of a work item (j counts the boxes the item
+// loads).  A half item loads BN/2 columns: for silu_mul tiles, whose columns
+// are [gate | up], the half takes the matching quarter of each.
+template <int BN, int kBoxN, bool kSiluMul>
+__device__ __forceinline__ int b_box_col(int nb, int half, int j) {
+  if (half < 0) return nb * BN + j * kBoxN;
+  if constexpr (kSiluMul) {
+    constexpr int kPerPart = BN / 4 / kBoxN;  // boxes per quarter
+    const int part = j / kPerPart;            // 0: gate, 1: up
+    return nb * BN + part * (BN / 2) + half * (BN / 4) + (j % kPerPart) * kBoxN;
+  }
+  return nb * BN + half * (BN / 2) + j * kBoxN;
+}
+
+// float4 index, within one unit's partial tile, of 16-byte group j (columns
+// 4j..4j+3 of 64-column chunk c) of the row held by `lane` of epilogue warp
+// wq (0..3).  Consecutive lanes are consecutive, so warp accesses coalesce.
+__device__ __forceinline__ int partial_index(int c, int wq, int j, int lane) {
+  return ((c * 4 + wq) * 16 + j) * 32 + lane;
 }
 
 __device__ __forceinline__ void epilogue_bar_sync() {
   asm volatile("bar.sync 1, 128;" ::: "memory");  // warps 2..5 only
+}
+
+// 16-byte asynchronous global -> shared copy (L2 only) and its completion.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+__device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void st_global_v4(float* p, uint32_t a, uint32_t b, uint32_t c,
@@ -206,6 +278,9 @@ __device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" 
 __device__ __forceinline__ void red_release_sys_add(unsigned* p, unsigned v) {
   asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void red_release_gpu_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -220,15 +295,17 @@ __device__ __forceinline__ int tile_owner(int tile, int world) {
 __device__ __forceinline__ void comm_bar_sync() {
   asm volatile("bar.sync 2, 128;" ::: "memory");  // warps 6..9 only
 }
-// Waits until *p >= target; bounded like the pipeline waits.
+// Waits until *p >= target; bounded like the pipeline waits (on a timeout:
+// raises *abort, ORs `code` into *status and returns false).
 __device__ __forceinline__ bool wait_at_least(const unsigned* p, unsigned target,
-                                              volatile int* abort, unsigned* status) {
+                                              volatile int* abort, unsigned* status,
+                                              unsigned code = kWdPeer) {
   const long long t0 = clock64();
   while (static_cast<int>(ld_acquire_sys(p) - target) < 0) {
     if (*abort) return false;
     if (clock64() - t0 > kWaitLimitCycles) {
       *abort = 1;
-      atomicOr(status, kWdPeer);
+      atomicOr(status, code);
       return false;
     }
   }
@@ -306,6 +383,7 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
   using L = TcLayout<BN, STAGES, Op::kBytes>;
   constexpr int kBK = L::kBK;
   constexpr int kUmmaK = OpShape<Op::kBytes>::kUmmaK;
+  const uint32_t idesc_half = (idesc & ~(0x3Fu << 17)) | (static_cast<uint32_t>(BN / 2 / 8) << 17);
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -365,18 +443,27 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
       for (int i = 0; ok && work_item(sched, i, w); ++i) {
         int mb, nb;
         tile_coords(w.tile, tiles_m, tiles_n, mb, nb);
+        const int nbox = (w.half < 0 ? BN : BN / 2) / L::kBoxN;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, wd, kWdProducer)) {
             ok = false;
             break;
           }
           const uint32_t fb = full_bar(stage);
-          mbar_arrive_expect_tx(fb, L::kStageBytes);
+          mbar_arrive_expect_tx(fb, L::kABytes + nbox * L::kBBox);
           tma_load_2d(sA + stage * L::kABytes, &tmA, kb * kBK, mb * kBM, fb);
+          // Straight-line issue (constant trip counts): a runtime loop here
+          // cost 8 % of whole-tile throughput on B200.
+          if (w.half < 0) {
 #pragma unroll
-          for (int j = 0; j < BN / L::kBoxN; ++j) {
-            tma_load_2d(sB + stage * L::kBBytes + j * L::kBBox, &tmB, nb * BN + j * L::kBoxN,
-                        kb * kBK, fb);
+            for (int j = 0; j < BN / L::kBoxN; ++j)
+              tma_load_2d(sB + stage * L::kBBytes + j * L::kBBox, &tmB, nb * BN + j * L::kBoxN,
+                          kb * kBK, fb);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 2 / L::kBoxN; ++j)
+              tma_load_2d(sB + stage * L::kBBytes + j * L::kBBox, &tmB,
+                          b_box_col<BN, L::kBoxN, kSiluMul>(nb, w.half, j), kb * kBK, fb);
           }
           ++issued;
           if (++stage == STAGES) {
@@ -413,6 +500,8 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        // A half item is one MMA of N = BN/2 over the boxes it loaded.
+        const uint32_t id = w.half < 0 ? idesc : idesc_half;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_bounded(full_bar(stage), phase, abort_flag, wd, kWdMma)) {
             ok = false;
@@ -427,7 +516,7 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
             // B: MN-major, advance kUmmaK K rows (atoms of 8 rows x 128 B).
             const uint64_t ad = sdesc_sw128(a0 + k * 32, 16, 1024);
             const uint64_t bd = sdesc_sw128(b0 + k * kUmmaK * 128, L::kBBox, 1024);
-            Op::mma(d_tmem, ad, bd, idesc, kb > w.kb0 || k > 0);
+            Op::mma(d_tmem, ad, bd, id, kb > w.kb0 || k > 0);
           }
           umma_commit(empty_bar(stage));
           if (++stage == STAGES) {
@@ -504,66 +593,159 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
                             static_cast<uint32_t>(acc * BN);
       const int row_in_tile = q * 32 + lane;
       const int store_y = mb * kBM + q * 32;
-      bool whole_done = false;
-      if constexpr (kSiluMul) {
-        if (w.unit < 0) {
-          // Columns [0, BN/2) of the accumulator are gate, [BN/2, BN) up.
-#pragma unroll 1
-          for (int c = 0; c < BN / 128; ++c) {
-            uint32_t g[64], u[64];
-            tmem_ld_32x32b_x32(trow + c * 64, g);
-            tmem_ld_32x32b_x32(trow + c * 64 + 32, g + 32);
-            tmem_ld_32x32b_x32(trow + BN / 2 + c * 64, u);
-            tmem_ld_32x32b_x32(trow + BN / 2 + c * 64 + 32, u + 32);
-            tmem_wait_ld();
-            if (c == BN / 128 - 1) {
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(tempty_bar(acc));
-            }
-            const int store_x = nb * kOutCols + c * 64;
-            if (store_x >= n_out || store_y >= M) continue;
-            float f[64];
-#pragma unroll
-            for (int j = 0; j < 64; ++j) f[j] = silu_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
-            store_chunk(f, store_x, store_y);
+      const int slot = w.tile - sched.split_begin;
+      // K-split unit: the unit that completes the tile (the last to arrive)
+      // sums all partials in split order; the others leave theirs in the
+      // workspace.  Learn which one this is before draining TMEM.
+      bool split_last = false;
+      if constexpr (!kFused) {
+        if (w.unit >= 0) {
+          if (warp == 2 && lane == 0) {
+            const unsigned prev = atomicAdd(&sched.counters[slot], 1u);
+            *last_flag = prev == static_cast<unsigned>(sched.splits - 1) ? 1 : 0;
           }
-          whole_done = true;
+          epilogue_bar_sync();
+          split_last = *last_flag != 0;
+          epilogue_bar_sync();  // last_flag is rewritten by the next unit
+          if (!split_last) {
+            // Partial layout [chunk][warp][16-byte group][lane]: each warp
+            // store (and the last unit's load) covers 512 contiguous bytes.
+            float* dst = sched.ws + static_cast<size_t>(w.unit) * kBM * BN;
+#pragma unroll 1
+            for (int c = 0; c < BN / 64; ++c) {
+              uint32_t r[64];
+              tmem_ld_32x32b_x32(trow + c * 64, r);
+              tmem_ld_32x32b_x32(trow + c * 64 + 32, r + 32);
+              tmem_wait_ld();
+              if constexpr (Op::kIntAcc) {
+#pragma unroll
+                for (int j = 0; j < 64; ++j)
+                  r[j] = __float_as_uint(static_cast<float>(static_cast<int>(r[j])));
+              }
+              if (c == BN / 64 - 1) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(tempty_bar(acc));
+              }
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                st_global_v4(dst + 4 * partial_index(c, warp - 2, j, lane), r[4 * j], r[4 * j + 1],
+                             r[4 * j + 2], r[4 * j + 3]);
+            }
+            // All four warps' rows are written: count the partial in.
+            __threadfence();
+            epilogue_bar_sync();
+            if (warp == 2 && lane == 0)
+              red_release_gpu_add(sched.counters + sched.units / sched.splits + slot, 1u);
+            if (++acc == 2) {
+              acc = 0;
+              acc_phase ^= 1u;
+            }
+            continue;
+          }
+          // Last arriver: the other S - 1 units have arrived, so they are
+          // running and about to publish their partials; wait (bounded).
+          if (warp == 2 && lane == 0)
+            *last_flag = wait_at_least(sched.counters + sched.units / sched.splits + slot,
+                                       static_cast<unsigned>(sched.splits - 1), abort_flag, wd,
+                                       kWdSplit)
+                             ? 1
+                             : 0;
+          epilogue_bar_sync();
+          const bool ready = *last_flag != 0;
+          epilogue_bar_sync();
+          if (!ready) break;
+          __threadfence();
         }
       }
-#pragma unroll 1
-      for (int c = 0; c < BN / 64 && !whole_done; ++c) {
+      // 64 accumulator columns [tcol, tcol + 64) of this lane's row as fp32;
+      // for the last K-split unit, the sum of all S partials in split order.
+      // The other units' partial rows are fetched with cp.async into the A/B
+      // stage ring - idle by now, since a K-split unit is always its CTA's
+      // last work item and its MMAs have consumed every stage - laid out
+      // [split][16-byte group][thread] so each warp access is contiguous.
+      auto acc_chunk = [&](int tcol, float (&f)[64]) {
         uint32_t r[64];
-        tmem_ld_32x32b_x32(trow + c * 64, r);
-        tmem_ld_32x32b_x32(trow + c * 64 + 32, r + 32);
+        tmem_ld_32x32b_x32(trow + tcol, r);
+        tmem_ld_32x32b_x32(trow + tcol + 32, r + 32);
         tmem_wait_ld();
-        if constexpr (Op::kIntAcc) {
-          // s32 accumulator -> fp32 (exact below 2^24 in magnitude).
 #pragma unroll
-          for (int j = 0; j < 64; ++j) r[j] = __float_as_uint(static_cast<float>(static_cast<int>(r[j])));
+        for (int j = 0; j < 64; ++j)
+          f[j] = Op::kIntAcc ? static_cast<float>(static_cast<int>(r[j])) : __uint_as_float(r[j]);
+        if (!split_last) return;
+        const int me = w.unit % sched.splits;
+        const uint32_t et = threadIdx.x - 64;  // 0..127
+        const size_t unit_stride = static_cast<size_t>(kBM) * BN;
+        const float* base = sched.ws + static_cast<size_t>(slot) * sched.splits * unit_stride;
+        auto slot_addr = [&](int sp, int j) { return sA + ((sp * 16 + j) * 128 + et) * 16; };
+#pragma unroll 1
+        for (int sp = 0; sp < sched.splits; ++sp) {
+          if (sp == me) continue;
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            cp_async16(slot_addr(sp, j),
+                       base + sp * unit_stride + 4 * partial_index(tcol / 64, warp - 2, j, lane));
         }
-        if (c == BN / 64 - 1) {
+        cp_async_wait_all();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+          for (int sp = 0; sp < sched.splits; ++sp) {
+            const float4 v = sp == me ? make_float4(f[4 * j], f[4 * j + 1], f[4 * j + 2], f[4 * j + 3])
+                                      : ld_shared_f4(slot_addr(sp, j));
+            if (sp == 0) {
+              sum = v;
+            } else {
+              sum.x += v.x;
+              sum.y += v.y;
+              sum.z += v.z;
+              sum.w += v.w;
+            }
+          }
+          f[4 * j] = sum.x;
+          f[4 * j + 1] = sum.y;
+          f[4 * j + 2] = sum.z;
+          f[4 * j + 3] = sum.w;
+        }
+      };
+      // Accumulator columns this item holds: BN, or BN / 2 for a half tile.
+      const int ncols = w.half < 0 ? BN : BN / 2;
+      bool chunks_done = false;
+      if constexpr (kSiluMul) {
+        // The accumulator holds [gate | up], ncols / 2 columns each.
+        const int nch = ncols / 128;
+#pragma unroll 1
+        for (int c = 0; c < nch; ++c) {
+          float g[64], u[64];
+          acc_chunk(c * 64, g);
+          acc_chunk(ncols / 2 + c * 64, u);
+          if (c == nch - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty_bar(acc));
+          }
+          const int store_x = nb * kOutCols + (w.half < 0 ? 0 : w.half * (kOutCols / 2)) + c * 64;
+          if (store_x >= n_out || store_y >= M) continue;
+#pragma unroll
+          for (int j = 0; j < 64; ++j) g[j] = silu_f(g[j]) * u[j];
+          store_chunk(g, store_x, store_y);
+        }
+        chunks_done = true;
+      }
+      const int nch = ncols / 64;
+#pragma unroll 1
+      for (int c = 0; c < nch && !chunks_done; ++c) {
+        float f[64];
+        acc_chunk(c * 64, f);
+        if (c == nch - 1) {
           // Accumulator fully read: hand it back to the MMA warp.
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(tempty_bar(acc));
         }
-        if constexpr (!kFused) {
-          if (w.unit >= 0) {
-            // K-split unit: keep the fp32 partial for the tile's last arriver.
-            float* dst =
-                sched.ws + (static_cast<size_t>(w.unit) * kBM + row_in_tile) * BN + c * 64;
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              st_global_v4(dst + 4 * j, r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
-            continue;
-          }
-        }
-        const int store_x = nb * BN + c * 64;
+        const int store_x = nb * BN + (w.half < 0 ? 0 : w.half * (BN / 2)) + c * 64;
         if (store_x >= N || store_y >= M) continue;  // box entirely outside C
-        float f[64];
-#pragma unroll
-        for (int j = 0; j < 64; ++j) f[j] = __uint_as_float(r[j]);
         if constexpr (kScaled) {
           const int row = mb * kBM + row_in_tile;
           const float sa = row < M ? __ldg(sc.sa + static_cast<size_t>(row) * sc.sa_step) : 0.f;
@@ -588,87 +770,6 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
         epilogue_bar_sync();
         if (warp == 2 && lane == 0)
           red_release_sys_add(ar.peer_counters[tile_owner(w.tile, ar.world)] + w.tile, 1u);
-      } else {
-        if (w.unit >= 0) {
-          // All four warps' partial rows are written; count this unit in.
-          __threadfence();
-          epilogue_bar_sync();
-          const int slot = w.tile - sched.split_begin;
-          if (warp == 2 && lane == 0) {
-            const unsigned prev = atomicAdd(&sched.counters[slot], 1u);
-            const bool last = prev == static_cast<unsigned>(sched.splits - 1);
-            if (last) sched.counters[slot] = 0u;  // ready for the next launch
-            *last_flag = last ? 1 : 0;
-          }
-          epilogue_bar_sync();
-          if (*last_flag) {
-            // Sum the S partial tiles (split order) and store the 16-bit tile.
-            // The 128 epilogue threads sweep the tile in float4 steps, so loads
-            // and stores are coalesced along rows.
-            __threadfence();
-            const int et = threadIdx.x - 64;  // 0..127
-            const size_t unit_stride = static_cast<size_t>(kBM) * BN;
-            const float* base = sched.ws + static_cast<size_t>(slot * sched.splits) * unit_stride;
-            constexpr int kF4 = kBM * kOutCols / 4;  // float4 slots of the output tile
-  #pragma unroll 1
-            for (int f0 = et; f0 < kF4; f0 += 4 * 128) {
-              float4 sum[4], sum_up[4];
-  #pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                sum[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-                sum_up[u] = sum[u];
-              }
-              for (int sp = 0; sp < sched.splits; ++sp) {
-                const float* part = base + sp * unit_stride;
-                float4 v[4], vu[4];
-  #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                  const int f = f0 + u * 128;
-                  const float* p = part + (f / (kOutCols / 4)) * BN + (f % (kOutCols / 4)) * 4;
-                  v[u] = __ldcg(reinterpret_cast<const float4*>(p));
-                  if constexpr (kSiluMul) vu[u] = __ldcg(reinterpret_cast<const float4*>(p + BN / 2));
-                }
-  #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                  sum[u].x += v[u].x;
-                  sum[u].y += v[u].y;
-                  sum[u].z += v[u].z;
-                  sum[u].w += v[u].w;
-                  if constexpr (kSiluMul) {
-                    sum_up[u].x += vu[u].x;
-                    sum_up[u].y += vu[u].y;
-                    sum_up[u].z += vu[u].z;
-                    sum_up[u].w += vu[u].w;
-                  }
-                }
-              }
-  #pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                const int f = f0 + u * 128;
-                const int gr = mb * kBM + f / (kOutCols / 4);
-                const int gc = nb * kOutCols + (f % (kOutCols / 4)) * 4;
-                if constexpr (kSiluMul) {
-                  sum[u].x = silu_f(sum[u].x) * sum_up[u].x;
-                  sum[u].y = silu_f(sum[u].y) * sum_up[u].y;
-                  sum[u].z = silu_f(sum[u].z) * sum_up[u].z;
-                  sum[u].w = silu_f(sum[u].w) * sum_up[u].w;
-                }
-                if (gr < M && gc < n_out) {  // n_out % 8 == 0: gc < n_out implies gc + 3 < n_out
-                  if constexpr (kScaled) {
-                    const float sa = __ldg(sc.sa + static_cast<size_t>(gr) * sc.sa_step);
-                    const float4 sb = load_sb4(sc, gc, N);
-                    sum[u].x = (sum[u].x * sa) * sb.x;
-                    sum[u].y = (sum[u].y * sa) * sb.y;
-                    sum[u].z = (sum[u].z * sa) * sb.z;
-                    sum[u].w = (sum[u].w * sa) * sb.w;
-                  }
-                  store4(C + static_cast<size_t>(gr) * n_out + gc, sum[u].x, sum[u].y, sum[u].z,
-                         sum[u].w);
-                }
-              }
-            }
-          }
-        }
       }
       if (++acc == 2) {
         acc = 0;
@@ -765,13 +866,18 @@ struct TcPlan {
   size_t counter_bytes;  // leading part of the workspace holding the counters
 };
 
-// Tile schedule for the device: whole tiles round-robin and - when a
-// workspace is available and the tile count leaves a partial last wave of
-// `rem` tiles - those tiles cut into S = min(4, sms / rem, kblocks / 4) K
-// splits, so the split units form one round over the SMs and the last wave
-// lasts about 1/S of a tile plus the partial-sum pass.
-// `bk` is the K block of the operand kind (64 16-bit or 128 8-bit elements).
-TcPlan plan_tc(int M, int N, int K, int BN, int bk, int sms, bool allow_split) {
+// Tile schedule for the device.  Whole tiles go round-robin over the SMs; a
+// partial last wave of `rem` tiles (or a single partial wave) is cut so that
+// it keeps more SMs busy:
+//   * rem <= sms / 4, K >= kSplitMinKblocks blocks, workspace given: each tile
+//     is cut along K into S = min(4, sms / rem) units whose fp32 partials the
+//     last-arriving unit sums (deterministically, in split order) - the tail
+//     lasts about 1/S of a tile plus the read of S - 1 partials;
+//   * otherwise rem <= sms / 2: each tile runs as two N halves on two SMs -
+//     the tail lasts half a tile, with no reduction and results identical to
+//     whole tiles;
+//   * otherwise the tail runs whole.
+TcPlan plan_tc(int M, int N, int K, int BN, int bk, int sms, bool allow_split, bool allow_halves) {
   TcPlan p{};
   TcSched& s = p.sched;
   s.tiles_m = (M + kBM - 1) / kBM;
@@ -780,30 +886,35 @@ TcPlan plan_tc(int M, int N, int K, int BN, int bk, int sms, bool allow_split) {
   s.kblocks = (K + bk - 1) / bk;
   const int full = s.num_tiles / sms;
   const int rem = s.num_tiles - full * sms;
+  p.grid = s.num_tiles < sms ? s.num_tiles : sms;
+  s.full_rounds = (s.num_tiles + p.grid - 1) / p.grid;
+  s.split_begin = s.num_tiles;
+  s.halves = 0;
+  s.splits = 1;
+  s.kb_per_split = s.kblocks;
+  s.units = 0;
+  if (rem == 0) return p;
   int S = 1;
-  if (allow_split && full >= 1 && rem > 0) {
-    S = kMaxSplits;
-    if (S > sms / rem) S = sms / rem;
-    if (S > s.kblocks / 4) S = s.kblocks / 4;
-    if (S < 1) S = 1;
-  }
-  if (S == 1) {
-    p.grid = s.num_tiles < sms ? s.num_tiles : sms;
-    s.full_rounds = (s.num_tiles + p.grid - 1) / p.grid;
-    s.split_begin = s.num_tiles;
-    s.splits = 1;
-    s.kb_per_split = s.kblocks;
-    s.units = 0;
+  if (allow_split && rem * kMaxSplits <= sms && s.kblocks >= kSplitMinKblocks) S = kMaxSplits;
+  if (S > 1) {
+    p.grid = sms;
+    s.full_rounds = full;
+    s.split_begin = full * sms;
+    s.kb_per_split = (s.kblocks + S - 1) / S;
+    s.splits = (s.kblocks + s.kb_per_split - 1) / s.kb_per_split;  // every split non-empty
+    s.units = rem * s.splits;
+    p.counter_bytes =
+        (2 * static_cast<size_t>(rem) * sizeof(unsigned) + 255) & ~static_cast<size_t>(255);
+    p.ws_bytes = p.counter_bytes + static_cast<size_t>(s.units) * kBM * BN * sizeof(float);
     return p;
   }
-  p.grid = sms;
-  s.full_rounds = full;
-  s.split_begin = full * sms;
-  s.kb_per_split = (s.kblocks + S - 1) / S;
-  s.splits = (s.kblocks + s.kb_per_split - 1) / s.kb_per_split;  // every split non-empty
-  s.units = rem * s.splits;
-  p.counter_bytes = (static_cast<size_t>(rem) * sizeof(unsigned) + 255) & ~static_cast<size_t>(255);
-  p.ws_bytes = p.counter_bytes + static_cast<size_t>(s.units) * kBM * BN * sizeof(float);
+  if (allow_halves && 2 * rem <= sms) {
+    p.grid = full > 0 ? sms : 2 * rem;
+    s.full_rounds = full;
+    s.split_begin = full * sms;
+    s.halves = 1;
+    s.units = 2 * rem;
+  }
   return p;
 }
 
@@ -828,9 +939,11 @@ int launch_tc(void* c, const void* a, const void* b, int M, int N, int K, void* 
   constexpr bool kFused = kEpi == kEpiAllReduce;
   auto kernel = gemm_tc_kernel<Op, T, BN, STAGES, kEpi>;
   if (int st = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), L::kAlloc, info)) return st;
-  TcPlan p = plan_tc(M, N, K, BN, L::kBK, info.sm_count, workspace != nullptr);
+  // The fused all-reduce counts whole tiles: its tail always runs whole.
+  constexpr bool kHalves = !kFused;
+  TcPlan p = plan_tc(M, N, K, BN, L::kBK, info.sm_count, workspace != nullptr, kHalves);
   if (p.ws_bytes > 0 && (ws_bytes < p.ws_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255)))
-    p = plan_tc(M, N, K, BN, L::kBK, info.sm_count, false);
+    p = plan_tc(M, N, K, BN, L::kBK, info.sm_count, false, kHalves);
   if (p.ws_bytes > 0) {
     p.sched.counters = static_cast<unsigned*>(workspace);
     p.sched.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + p.counter_bytes);
@@ -866,7 +979,7 @@ constexpr int kTcStages = 4;
 size_t gemm_tc_workspace_size(int64_t M, int64_t N, int64_t K, int sm_count) {
   if (M <= 0 || N <= 0 || K <= 0 || M >= (1LL << 31) || N >= (1LL << 31) || K >= (1LL << 31))
     return 0;
-  return plan_tc((int)M, (int)N, (int)K, kTcBN, OpShape<2>::kBK, sm_count, true).ws_bytes;
+  return plan_tc((int)M, (int)N, (int)K, kTcBN, OpShape<2>::kBK, sm_count, true, true).ws_bytes;
 }
 
 int gemm_tc(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K, int dtype,
@@ -906,7 +1019,7 @@ int gemm_silu_mul(void* act, const void* a, const void* b, int64_t M, int64_t N2
 size_t gemm_scaled_tc_workspace_size(int64_t M, int64_t N, int64_t K, int sm_count) {
   if (M <= 0 || N <= 0 || K <= 0 || M >= (1LL << 31) || N >= (1LL << 31) || K >= (1LL << 31))
     return 0;
-  return plan_tc((int)M, (int)N, (int)K, kTcBN, OpShape<1>::kBK, sm_count, true).ws_bytes;
+  return plan_tc((int)M, (int)N, (int)K, kTcBN, OpShape<1>::kBK, sm_count, true, true).ws_bytes;
 }
 
 namespace {

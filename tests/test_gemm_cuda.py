@@ -200,14 +200,23 @@ def test_full_size_sampled_rows(shape):
 
 # ---- K-split last wave (aotk_gemm_opt_ws) ----
 
-SPLIT_SHAPES = [(2560, 1024, 2048), (2560, 2048, 2048), (4096, 4096, 4096), (4096, 8192, 7168)]
+# (M, K, N) whose tail is cut along K on a 148-SM B200: 8, 22, 8 tiles left
+# after whole waves (K = 8192), a single partial wave of 16 tiles, and a
+# ragged single wave of 32 tiles.
+SPLIT_SHAPES = [(2048, 8192, 14336), (1280, 8192, 4352), (4096, 8192, 7168), (256, 8192, 2048),
+                (1000, 8192, 1000)]
+# (M, K, N) whose tail runs as N halves: 68, 16 and 12 tiles left (K too short
+# to split), and single partial waves of 9 and 64 tiles.
+HALF_SHAPES = [(4096, 4096, 4096), (2048, 4096, 28672), (2560, 1024, 2048), (300, 328, 768),
+               (1024, 2048, 2048)]
 
 
 @pytest.mark.parametrize("shape", SPLIT_SHAPES, ids=str)
 def test_split_last_wave_matches_oracle(shape):
-    """Shapes whose tile count leaves a partial last wave: the leftover tiles
-    are computed in K splits through a workspace and must match the oracle,
-    be bit-identical across calls, and not depend on the workspace contents."""
+    """Shapes whose tile count leaves a small partial last wave: the leftover
+    tiles are computed in K splits through a workspace and must match the
+    oracle, be bit-identical across calls, and not depend on the workspace
+    contents."""
     import torch
 
     from aot_kernel import capi
@@ -233,13 +242,39 @@ def test_split_last_wave_matches_oracle(shape):
     assert capi.watchdog_status() == 0
 
 
+@pytest.mark.parametrize("shape", HALF_SHAPES, ids=str)
+def test_half_tile_tail_matches_oracle(shape):
+    """Tails run as two N halves per tile need no workspace: compared with the
+    oracle on sampled rows and the last row block, and with an fp32 torch
+    matmul of the same inputs on every element."""
+    import torch
+
+    from aot_kernel import capi
+
+    M, K, N = shape
+    a, b = _inputs(M, K, N, "bfloat16", seed=M + 5 * N, b_std=K ** -0.5)
+    ta, tb = to_device(a, "bfloat16"), to_device(b, "bfloat16")
+    assert capi.gemm_opt_workspace_size(M, N, K, capi.BFLOAT16) == 0
+    c = torch.empty((M, N), device="cuda", dtype=torch.bfloat16)
+    capi.gemm_tc(c, ta, tb, M, N, K, capi.BFLOAT16)
+    rows = np.unique(np.concatenate([np.random.default_rng(3).integers(0, M, size=48),
+                                     np.arange(max(0, M - 128), M, 5)]))
+    expect = ops.gemm(a[rows], b, "bfloat16")
+    assert_close_for_gemm(c[torch.as_tensor(rows, device="cuda")], expect, "bfloat16")
+    torch.backends.cuda.matmul.allow_tf32 = False
+    full = (ta.float() @ tb.float()).to(torch.bfloat16)
+    torch.cuda.synchronize()
+    assert_close_for_gemm(c, full, "bfloat16")
+    assert capi.watchdog_status() == 0
+
+
 def test_split_and_whole_schedules_agree():
     import torch
 
     import aot_kernel
     from aot_kernel import capi
 
-    M, K, N = 4096, 4096, 4096
+    M, K, N = 1280, 8192, 4352
     a, b = _inputs(M, K, N, "bfloat16", seed=77, b_std=K ** -0.5)
     ta, tb = to_device(a, "bfloat16"), to_device(b, "bfloat16")
     whole = torch.empty((M, N), device="cuda", dtype=torch.bfloat16)
@@ -255,8 +290,9 @@ def test_split_and_whole_schedules_agree():
 @pytest.mark.parametrize("shape", [(256, 512, 256), (300, 328, 384), (2560, 1024, 1024),
                                    (4096, 8192, 3584)], ids=str)
 def test_gemm_silu_mul_matches_oracle(shape):
-    """(M, K, I): interleaved [K, 2I] weight, act [M, I]; the last two shapes
-    leave a partial last wave (K-split path with the fused finalize)."""
+    """(M, K, I): interleaved [K, 2I] weight, act [M, I]; the tails of the
+    first three run as N halves (each half keeps matching gate and up
+    columns), the last leaves 8 tiles cut along K (fused finalize)."""
     import torch
 
     import aot_kernel

@@ -237,10 +237,10 @@ def test_scaled_gemm_tc_output_dtypes(qdtype, out):
 
 
 @pytest.mark.parametrize("qdtype", ["e4m3", "int8"])
-def test_scaled_gemm_tc_k_split_last_wave(qdtype):
-    """160 tiles of 128 x 256 on 148 SMs: the 12 tiles of the last wave are cut
-    along K into 4 units each and reduced from the workspace (deterministic:
-    two runs agree bit for bit)."""
+def test_scaled_gemm_tc_k_split_tail(qdtype):
+    """8 tiles of 128 x 256 on 148 SMs with K = 16384 (128 K blocks of 128):
+    each tile is cut along K into 4 units whose partials the last unit sums
+    from the workspace (deterministic: two runs agree bit for bit)."""
     import torch
 
     from aot_kernel import capi
@@ -248,7 +248,7 @@ def test_scaled_gemm_tc_k_split_last_wave(qdtype):
     props = torch.cuda.get_device_properties(0)
     if props.multi_processor_count != 148:
         pytest.skip("tile arithmetic assumes 148 SMs")
-    M, K, N = 2048, 2048, 2560
+    M, K, N = 256, 16384, 1024
     assert capi.scaled_gemm_workspace_size(M, N, K, capi.dtype_code(_qtorch(qdtype))) > 0
     got, a_q, b_q, sa, sb = _capi_run("tc", M, K, N, qdtype, "bfloat16", "row", seed=21,
                                       workspace=True)
