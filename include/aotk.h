@@ -150,6 +150,27 @@ AOTK_API int aotk_gemm_opt_workspace_size(int64_t M, int64_t N, int64_t K, int d
 AOTK_API int aotk_gemm_opt_noalloc(void* c, const void* a, const void* b, int64_t M, int64_t N,
                                    int64_t K, int dtype, void* stream);
 
+/* aotk_gemm_opt on host-resident operands: c_host[M, N] = a_host[M, K] *
+ * b_host[K, N], FLOAT16 / BFLOAT16, through caller-provided device buffers
+ * a_dev [M, K], b_dev [K, N], c_dev [M, N] of the same dtype.  B is copied in
+ * first, then A in blocks of 128-row multiples (about eight); the GEMM of
+ * block i runs on `stream` as soon as its rows have landed while the next
+ * block is still in flight, and block i of C is copied out while later blocks
+ * compute, so inbound copies, GEMMs and outbound copies overlap.  Host
+ * buffers should be page-locked for the copies to run asynchronously.  The
+ * call is ordered on `stream` like one operation: work queued on `stream`
+ * before it completes before its copies start, and work queued after it sees
+ * c_host filled once the stream reaches it (synchronise before reading
+ * c_host on the host).  Two copy streams and a few events per device are
+ * created on first use and kept.  workspace as for aotk_gemm_opt_ws, sized by
+ * aotk_gemm_host_workspace_size (NULL / 0: none).  No reference counterpart:
+ * the reference's callers copy with torch and call gemm. */
+AOTK_API int aotk_gemm_host(void* c_host, const void* a_host, const void* b_host, int64_t M,
+                            int64_t N, int64_t K, int dtype, void* a_dev, void* b_dev, void* c_dev,
+                            void* workspace, size_t workspace_bytes, void* stream);
+AOTK_API int aotk_gemm_host_workspace_size(int64_t M, int64_t N, int64_t K, int dtype,
+                                           size_t* bytes);
+
 /* Any-dtype, any-shape GEMM (SIMT, fp32 accumulation).
  * Replaces gemm(Tensor! out, Tensor a, Tensor b)
  * (aot_kernel/csrc/gemm/gemm.cu:106-157, registration.cc:20-21). */

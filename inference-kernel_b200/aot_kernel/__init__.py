@@ -11,7 +11,7 @@ are new fused ops; ``scaled_gemm`` is the reference's 8-bit GEMM
 """
 
 from .activation import relu, silu, silu_mul
-from .gemm import gemm, gemm_naive, gemm_silu_mul, interleave_gate_up, scaled_gemm
+from .gemm import gemm, gemm_host, gemm_naive, gemm_silu_mul, interleave_gate_up, scaled_gemm
 from .norm import add_rmsnorm, rms_norm, rmsnorm
 
 __version__ = "0.1.0"
@@ -19,6 +19,7 @@ __version__ = "0.1.0"
 __all__ = [
     "add_rmsnorm",
     "gemm",
+    "gemm_host",
     "gemm_naive",
     "gemm_silu_mul",
     "interleave_gate_up",

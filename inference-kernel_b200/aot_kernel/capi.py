@@ -47,6 +47,9 @@ SIGNATURES: dict[str, list] = {
     "aotk_gemm_silu_mul": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr, ctypes.c_size_t, _ptr],
     "aotk_gemm_silu_mul_workspace_size": [_i64, _i64, _i64, _int, ctypes.POINTER(ctypes.c_size_t)],
     "aotk_gemm_allreduce": [_ptr, _ptr, _i64, _i64, _i64, _int, ctypes.c_void_p, _ptr],
+    "aotk_gemm_host": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr, _ptr, _ptr, _ptr,
+                       ctypes.c_size_t, _ptr],
+    "aotk_gemm_host_workspace_size": [_i64, _i64, _i64, _int, ctypes.POINTER(ctypes.c_size_t)],
     "aotk_scaled_gemm": [_ptr, _ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _int, _int, _ptr,
                          ctypes.c_size_t, _ptr],
     "aotk_scaled_gemm_workspace_size": [_i64, _i64, _i64, _int, ctypes.POINTER(ctypes.c_size_t)],
@@ -217,6 +220,18 @@ def gemm_silu_mul(act, a, b_gate_up, M, I, K, dtype, workspace=None, workspace_b
                   stream=None) -> None:
     _call("aotk_gemm_silu_mul", _p(act), _p(a), _p(b_gate_up), M, I, K, dtype, _p(workspace),
           workspace_bytes, _stream(stream))
+
+
+def gemm_host_workspace_size(M, N, K, dtype) -> int:
+    n = ctypes.c_size_t(0)
+    _call("aotk_gemm_host_workspace_size", M, N, K, dtype, ctypes.byref(n))
+    return n.value
+
+
+def gemm_host(c_host, a_host, b_host, M, N, K, dtype, a_dev, b_dev, c_dev, workspace=None,
+              workspace_bytes=0, stream=None) -> None:
+    _call("aotk_gemm_host", _p(c_host), _p(a_host), _p(b_host), M, N, K, dtype, _p(a_dev),
+          _p(b_dev), _p(c_dev), _p(workspace), workspace_bytes, _stream(stream))
 
 
 def scaled_gemm_workspace_size(M, N, K, in_dtype) -> int:

@@ -52,6 +52,48 @@ def gemm_naive(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def gemm_host(a: torch.Tensor, b: torch.Tensor, *, out: torch.Tensor | None = None,
+              device: torch.device | int | None = None) -> torch.Tensor:
+    """C = A @ B for fp16/bf16 matrices in HOST memory, on the current (or
+    given) CUDA device, through the C ABI entry ``aotk_gemm_host``: B and row
+    blocks of A are copied in while earlier blocks compute and finished blocks
+    of C are copied out, so the PCIe link runs both directions during the
+    GEMM.  ``a`` / ``b`` / ``out`` should be pinned (``pin_memory()``) for the
+    copies to overlap; ``out`` defaults to a new pinned [M, N] tensor.  The
+    result is complete when this returns (the call synchronises its stream).
+    Not in the reference, whose callers copy with torch and call ``gemm``."""
+    from . import capi
+
+    if a.is_cuda or b.is_cuda:
+        raise ValueError("gemm_host takes host tensors; use gemm for device tensors")
+    assert_contiguous(a, b)
+    dtype = assert_same_dtype(a, b)
+    if dtype not in _TENSOR_CORE_DTYPES:
+        raise ValueError(f"gemm_host supports fp16/bf16, got {dtype}")
+    if a.dim() != 2 or b.dim() != 2 or a.size(1) != b.size(0):
+        raise ValueError(f"gemm_host expects a [M, K] and b [K, N], got {tuple(a.shape)} {tuple(b.shape)}")
+    M, K = a.shape
+    N = b.size(1)
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                       torch.device("cuda", device).index)
+    if out is None:
+        out = torch.empty((M, N), dtype=dtype, pin_memory=True)
+    elif out.is_cuda or tuple(out.shape) != (M, N) or out.dtype != dtype or not out.is_contiguous():
+        raise ValueError("out must be a contiguous host tensor of shape [M, N] and the inputs' dtype")
+    code = capi.dtype_code(dtype)
+    with torch.cuda.device(dev):
+        a_d = torch.empty((M, K), dtype=dtype, device=dev)
+        b_d = torch.empty((K, N), dtype=dtype, device=dev)
+        c_d = torch.empty((M, N), dtype=dtype, device=dev)
+        nbytes = capi.gemm_host_workspace_size(M, N, K, code)
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
+        stream = torch.cuda.current_stream(dev)
+        capi.gemm_host(out, a, b, M, N, K, code, a_d, b_d, c_d, ws if nbytes else None, nbytes,
+                       stream.cuda_stream)
+        stream.synchronize()
+    return out
+
+
 GATE_UP_BLOCK = 128  # column block of the interleaved gate/up layout
 
 

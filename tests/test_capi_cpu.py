@@ -64,6 +64,13 @@ def test_version():
                                        capi.SCALE_ROW), capi.ERR_INVALID_ARGUMENT),
         (lambda: capi.scaled_gemm_tc(16, 16, 16, 16, 16, 4, 4, 0, capi.FLOAT8_E5M2, capi.FLOAT16,
                                      capi.SCALE_ROW), capi.ERR_INVALID_ARGUMENT),  # empty K
+        # host-buffer GEMM: fp32, null device buffer, negative size
+        (lambda: capi.gemm_host(16, 16, 16, 4, 4, 4, capi.FLOAT32, 16, 16, 16),
+         capi.ERR_UNSUPPORTED),
+        (lambda: capi.gemm_host(16, 16, 16, 4, 4, 4, capi.BFLOAT16, None, 16, 16),
+         capi.ERR_INVALID_ARGUMENT),
+        (lambda: capi.gemm_host(16, 16, 16, -4, 4, 4, capi.BFLOAT16, 16, 16, 16),
+         capi.ERR_INVALID_ARGUMENT),
     ],
 )
 def test_argument_errors_without_device(call, status):
@@ -79,6 +86,7 @@ def test_empty_problems_are_no_ops():
     capi.rmsnorm_forward(0, 0, 0, 0, 4096, 1e-6, capi.BFLOAT16)
     capi.silu_mul_forward(0, 0, 0, 0, 0, 0, 0, 16, capi.BFLOAT16)
     capi.scaled_gemm(0, 0, 0, 0, 0, 0, 16, 16, capi.INT8, capi.BFLOAT16, capi.SCALE_TENSOR)
+    capi.gemm_host(0, 0, 0, 0, 16, 16, capi.BFLOAT16, 0, 0, 0)
     assert capi.scaled_gemm_workspace_size(256, 250, 256, capi.FLOAT8_E4M3) == 0  # N % 16 != 0
 
 

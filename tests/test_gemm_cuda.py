@@ -268,6 +268,27 @@ def test_half_tile_tail_matches_oracle(shape):
     assert capi.watchdog_status() == 0
 
 
+def test_half_tiles_equal_whole_tiles():
+    """A tail tile run as two N halves (MMA N = 128) gives the same bits as the
+    same tile run whole (N = 256): 4096^3 leaves 68 tail tiles (halves);
+    the same rows computed as two 2048-row GEMMs (256 tiles: one wave and
+    108 whole tiles) must agree exactly."""
+    import torch
+
+    from aot_kernel import capi
+
+    M, K, N = 4096, 4096, 4096
+    a, b = _inputs(M, K, N, "bfloat16", seed=31, b_std=K ** -0.5)
+    ta, tb = to_device(a, "bfloat16"), to_device(b, "bfloat16")
+    halves = torch.empty((M, N), device="cuda", dtype=torch.bfloat16)
+    capi.gemm_tc(halves, ta, tb, M, N, K, capi.BFLOAT16)
+    whole = torch.empty_like(halves)
+    for r0 in (0, M // 2):
+        capi.gemm_tc(whole[r0:r0 + M // 2], ta[r0:r0 + M // 2], tb, M // 2, N, K, capi.BFLOAT16)
+    torch.cuda.synchronize()
+    assert torch.equal(halves, whole)
+
+
 def test_split_and_whole_schedules_agree():
     import torch
 
@@ -315,3 +336,50 @@ def test_gemm_silu_mul_matches_oracle(shape):
     up = aot_kernel.gemm(ta, to_device(wu, "bfloat16"))
     ref2 = aot_kernel.silu_mul(gate, up)
     assert_close_for_gemm(act, ref2, "bfloat16")
+
+
+# ---- host-resident operands (aot_kernel.gemm_host / aotk_gemm_host) ----
+
+@pytest.mark.parametrize("shape", [(1000, 512, 776), (3000, 1024, 2048), (100, 256, 512),
+                                   (2048, 4096, 4096)], ids=str)
+@pytest.mark.parametrize("pinned", [True, False], ids=["pinned", "pageable"])
+def test_gemm_host_matches_oracle(shape, pinned):
+    """Row blocks of A (a remainder block, a single block, eight full blocks)
+    streamed in while earlier blocks compute; pageable buffers stay correct."""
+    import torch
+
+    import aot_kernel
+
+    M, K, N = shape
+    a, b = _inputs(M, K, N, "bfloat16", seed=M + K + N, b_std=K ** -0.5)
+    ta = torch.from_numpy(a).to(torch.bfloat16)
+    tb = torch.from_numpy(b).to(torch.bfloat16)
+    if pinned:
+        ta, tb = ta.pin_memory(), tb.pin_memory()
+    c = aot_kernel.gemm_host(ta, tb)
+    assert not c.is_cuda and tuple(c.shape) == (M, N)
+    rows = np.unique(np.concatenate([np.random.default_rng(5).integers(0, M, size=40),
+                                     np.arange(max(0, M - 130), M, 3)]))
+    assert_close_for_gemm(c[torch.as_tensor(rows)], ops.gemm(a[rows], b, "bfloat16"), "bfloat16")
+
+
+def test_gemm_host_through_c_abi_on_a_side_stream():
+    import torch
+
+    from aot_kernel import capi
+
+    M, K, N = 1536, 1024, 1024
+    a, b = _inputs(M, K, N, "bfloat16", seed=9, b_std=K ** -0.5)
+    ta = torch.from_numpy(a).to(torch.bfloat16).pin_memory()
+    tb = torch.from_numpy(b).to(torch.bfloat16).pin_memory()
+    c = torch.full((M, N), float("nan"), dtype=torch.bfloat16).pin_memory()
+    a_d = torch.empty((M, K), dtype=torch.bfloat16, device="cuda")
+    b_d = torch.empty((K, N), dtype=torch.bfloat16, device="cuda")
+    c_d = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    side = torch.cuda.Stream()
+    for _ in range(2):  # the second call reuses the device buffers after the first
+        capi.gemm_host(c, ta, tb, M, N, K, capi.BFLOAT16, a_d, b_d, c_d, stream=side.cuda_stream)
+    side.synchronize()
+    assert not torch.isnan(c).any()
+    rows = np.arange(0, M, 37)
+    assert_close_for_gemm(c[torch.as_tensor(rows)], ops.gemm(a[rows], b, "bfloat16"), "bfloat16")
