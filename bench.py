@@ -81,6 +81,9 @@ def parse_args():
                     help="down projection + all-reduce: NCCL after the GEMM, or one fused kernel")
     ap.add_argument("--tp-unfused-silu", action="store_true",
                     help="gate/up GEMM then silu_mul, instead of the fused gate/up + silu kernel")
+    ap.add_argument("--tp-unfolded-norm", action="store_true",
+                    help="run rms_norm as its own kernel instead of folding it into the fused "
+                         "gate/up kernel (norm weight in the weight rows, rstd in the epilogue)")
     ap.add_argument("--case", choices=sorted(CASES), default=None,
                     help="run only this workload's launches (for profilers)")
     return ap.parse_args()
@@ -475,22 +478,26 @@ def tp_mlp(args, rank: int, world: int, peaks: dict) -> dict:
     import torch.distributed as dist
 
     from aot_kernel.tp_mlp import (MLPShard, TensorParallelMLP, shard_down, shard_gate_up,
-                                   shard_gate_up_interleaved)
+                                   shard_gate_up_folded, shard_gate_up_interleaved)
 
     T, H, inter = 4096, 8192, 28672
     x = rand_bf16((T, H), 30)
     nw = rand_bf16((H,), 31, std=0.1, mean=1.0)
     w_gu = rand_bf16((H, 2 * inter), 32, std=0.02)
     fused_silu = not args.tp_unfused_silu
-    wgu_r = (shard_gate_up_interleaved if fused_silu else shard_gate_up)(w_gu, rank, world)
+    fold_norm = fused_silu and not args.tp_unfolded_norm
+    if fold_norm:
+        wgu_r = shard_gate_up_folded(w_gu, nw, rank, world)
+    else:
+        wgu_r = (shard_gate_up_interleaved if fused_silu else shard_gate_up)(w_gu, rank, world)
     del w_gu
     w_d = rand_bf16((inter, H), 33, std=0.02)
     wd_r = shard_down(w_d, rank, world)
     del w_d
     torch.cuda.empty_cache()
     allreduce = args.tp_allreduce if world > 1 else "nccl"
-    block = TensorParallelMLP(MLPShard(nw, wgu_r, wd_r, fused_silu=fused_silu), eps=1e-6,
-                              chunks=args.tp_chunks, allreduce=allreduce)
+    block = TensorParallelMLP(MLPShard(nw, wgu_r, wd_r, fused_silu=fused_silu, fold_norm=fold_norm),
+                              eps=1e-6, chunks=args.tp_chunks, allreduce=allreduce)
     for _ in range(max(3, args.warmup)):
         block(x)
     torch.cuda.synchronize()
@@ -514,6 +521,7 @@ def tp_mlp(args, rank: int, world: int, peaks: dict) -> dict:
     return {"tokens_per_s": T / (ms * 1e-3), "ms_per_step": ms, "tokens": T, "hidden": H,
             "intermediate": inter, "tp": world, "chunks": args.tp_chunks,
             "allreduce": allreduce if world > 1 else None, "fused_silu": fused_silu,
+            "fold_norm": fold_norm,
             "gpu_launches_per_step": (2 if fused_silu else 3)
             + (1 if world == 1 or allreduce == "fused" else args.tp_chunks),
             "tensor_frac_per_gpu": per_gpu_ideal_ms / ms, "allreduce_bytes": T * H * 2,
@@ -530,7 +538,11 @@ def tp_phase_breakdown(block, x, world: int, reps: int = 5) -> dict:
     ops, s = block.ops, block.shard
     fused = world > 1 and block.allreduce == "fused"
     fsilu = s.fused_silu
-    names = ["rms_norm"] + (["gemm_gate_up+silu_mul (fused)"] if fsilu else ["gemm_gate_up", "silu_mul"])
+    if s.fold_norm:
+        names = ["rms_rstd", "gemm_gate_up+rms_norm+silu_mul (fused)"]
+    else:
+        names = ["rms_norm"] + (["gemm_gate_up+silu_mul (fused)"] if fsilu else
+                                ["gemm_gate_up", "silu_mul"])
     names += ["gemm_down+all_reduce (fused)"] if fused else ["gemm_down", "all_reduce"]
     acc = torch.zeros(len(names), dtype=torch.float64, device="cuda")
     for _ in range(reps):
@@ -541,12 +553,20 @@ def tp_phase_breakdown(block, x, world: int, reps: int = 5) -> dict:
         torch.cuda._sleep(2_000_000)
         i = 0
         ev[i].record()
-        h = ops.rms_norm(x, s.norm_weight, block.eps)
-        i += 1
-        ev[i].record()
-        if fsilu:
+        if s.fold_norm:
+            rstd = ops.rms_rstd(x, block.eps)
+            i += 1
+            ev[i].record()
+            act = ops.gemm_silu_mul(x, s.w_gate_up, rstd)
+        elif fsilu:
+            h = ops.rms_norm(x, s.norm_weight, block.eps)
+            i += 1
+            ev[i].record()
             act = ops.gemm_silu_mul(h, s.w_gate_up)
         else:
+            h = ops.rms_norm(x, s.norm_weight, block.eps)
+            i += 1
+            ev[i].record()
             gu = ops.gemm(h, s.w_gate_up)
             i += 1
             ev[i].record()

@@ -106,6 +106,13 @@ AOTK_API int aotk_add_rmsnorm_forward(void* out, void* residual_out, const void*
                                       const void* residual, const void* weight, int64_t rows,
                                       int64_t cols, double eps, int dtype, void* stream);
 
+/* rstd[r] = rsqrt(mean(x[r, :]^2) + eps) in fp32 (rms_norm's row statistic,
+ * for folding the normalisation into the next GEMM: see
+ * aotk_gemm_silu_mul_rowscale).  x is [rows, cols] dense; one read of x.  No
+ * reference counterpart. */
+AOTK_API int aotk_rmsnorm_rstd(float* rstd, const void* x, int64_t rows, int64_t cols, double eps,
+                               int dtype, void* stream);
+
 /* ---- gemm ------------------------------------------------------------- */
 
 /* Tensor-core GEMM for FLOAT16 / BFLOAT16 (FLOAT32 returns AOTK_ERR_UNSUPPORTED,
@@ -218,6 +225,20 @@ AOTK_API int aotk_gemm_silu_mul(void* act, const void* a, const void* b_gate_up,
                                 size_t workspace_bytes, void* stream);
 AOTK_API int aotk_gemm_silu_mul_workspace_size(int64_t M, int64_t I, int64_t K, int dtype,
                                                size_t* bytes);
+
+/* aotk_gemm_silu_mul with a per-row scale of both projections:
+ * act[m, :] = silu(s_m (A @ W_gate)[m, :]) * (s_m (A @ W_up)[m, :]), s =
+ * row_scale[M] fp32.  With A = x, s = rstd from aotk_rmsnorm_rstd and the
+ * norm weight folded into the rows of the gate/up weight (W' = diag(w) W,
+ * rounded once), this is the gate/up projection of rms_norm(x, w) without
+ * the normalised activations ever being written: rms_norm as the GEMM's
+ * prologue.  Numerically it differs from the unfused composition by where
+ * the roundings fall (W' instead of the normalised x).  Same layout and
+ * preconditions as aotk_gemm_silu_mul.  No reference counterpart. */
+AOTK_API int aotk_gemm_silu_mul_rowscale(void* act, const void* a, const void* b_gate_up,
+                                         const float* row_scale, int64_t M, int64_t I, int64_t K,
+                                         int dtype, void* workspace, size_t workspace_bytes,
+                                         void* stream);
 
 /* ---- scaled (dequantising) 8-bit gemm ----------------------------------- */
 

@@ -11,13 +11,15 @@ are new fused ops; ``scaled_gemm`` is the reference's 8-bit GEMM
 """
 
 from .activation import relu, silu, silu_mul
-from .gemm import gemm, gemm_host, gemm_naive, gemm_silu_mul, interleave_gate_up, scaled_gemm
-from .norm import add_rmsnorm, rms_norm, rmsnorm
+from .gemm import (fold_norm_weight, gemm, gemm_host, gemm_naive, gemm_silu_mul,
+                   interleave_gate_up, scaled_gemm)
+from .norm import add_rmsnorm, rms_norm, rms_rstd, rmsnorm
 
 __version__ = "0.1.0"
 
 __all__ = [
     "add_rmsnorm",
+    "fold_norm_weight",
     "gemm",
     "gemm_host",
     "gemm_naive",
@@ -25,6 +27,7 @@ __all__ = [
     "interleave_gate_up",
     "relu",
     "rms_norm",
+    "rms_rstd",
     "rmsnorm",
     "scaled_gemm",
     "silu",

@@ -47,6 +47,9 @@ SIGNATURES: dict[str, list] = {
     "aotk_gemm_silu_mul": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr, ctypes.c_size_t, _ptr],
     "aotk_gemm_silu_mul_workspace_size": [_i64, _i64, _i64, _int, ctypes.POINTER(ctypes.c_size_t)],
     "aotk_gemm_allreduce": [_ptr, _ptr, _i64, _i64, _i64, _int, ctypes.c_void_p, _ptr],
+    "aotk_rmsnorm_rstd": [_ptr, _ptr, _i64, _i64, ctypes.c_double, _int, _ptr],
+    "aotk_gemm_silu_mul_rowscale": [_ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr,
+                                    ctypes.c_size_t, _ptr],
     "aotk_gemm_host": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr, _ptr, _ptr, _ptr,
                        ctypes.c_size_t, _ptr],
     "aotk_gemm_host_workspace_size": [_i64, _i64, _i64, _int, ctypes.POINTER(ctypes.c_size_t)],
@@ -220,6 +223,16 @@ def gemm_silu_mul(act, a, b_gate_up, M, I, K, dtype, workspace=None, workspace_b
                   stream=None) -> None:
     _call("aotk_gemm_silu_mul", _p(act), _p(a), _p(b_gate_up), M, I, K, dtype, _p(workspace),
           workspace_bytes, _stream(stream))
+
+
+def rmsnorm_rstd(rstd, x, rows: int, cols: int, eps: float, dtype: int, stream=None) -> None:
+    _call("aotk_rmsnorm_rstd", _p(rstd), _p(x), rows, cols, eps, dtype, _stream(stream))
+
+
+def gemm_silu_mul_rowscale(act, a, b_gate_up, row_scale, M, I, K, dtype, workspace=None,
+                           workspace_bytes=0, stream=None) -> None:
+    _call("aotk_gemm_silu_mul_rowscale", _p(act), _p(a), _p(b_gate_up), _p(row_scale), M, I, K,
+          dtype, _p(workspace), workspace_bytes, _stream(stream))
 
 
 def gemm_host_workspace_size(M, N, K, dtype) -> int:

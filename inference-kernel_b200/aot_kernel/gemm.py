@@ -110,16 +110,37 @@ def interleave_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor
     return torch.cat([g, u], dim=2).reshape(K, 2 * inter).contiguous()
 
 
-def gemm_silu_mul(a: torch.Tensor, w_gate_up: torch.Tensor) -> torch.Tensor:
+def gemm_silu_mul(a: torch.Tensor, w_gate_up: torch.Tensor,
+                  row_scale: torch.Tensor | None = None) -> torch.Tensor:
     """silu(a @ W_gate) * (a @ W_up) in one kernel; ``w_gate_up`` from
     ``interleave_gate_up``.  The gate/up product stays in TMEM: silu and the
-    product use the fp32 accumulators and the result is rounded once."""
+    product use the fp32 accumulators and the result is rounded once.
+
+    With ``row_scale`` (fp32 [M]) both products of row m are scaled by
+    row_scale[m] before silu: with a = x, row_scale = ``rms_rstd(x)`` and
+    ``fold_norm_weight(w_gate_up, norm_w)``, this is the gate/up projection
+    of ``rms_norm(x, norm_w)`` with the normalisation folded into the GEMM."""
     device, dtype = _validate(a, w_gate_up)
     if dtype not in _TENSOR_CORE_DTYPES:
         raise ValueError(f"gemm_silu_mul supports fp16/bf16, got {dtype}")
     out = torch.empty((a.size(0), w_gate_up.size(1) // 2), device=device, dtype=dtype)
-    torch.ops.aot_kernel.gemm_silu_mul(out, a, w_gate_up)
+    if row_scale is None:
+        torch.ops.aot_kernel.gemm_silu_mul(out, a, w_gate_up)
+    else:
+        torch.ops.aot_kernel.gemm_silu_mul_rowscale(out, a, w_gate_up,
+                                                    row_scale.reshape(-1).contiguous())
     return out
+
+
+def fold_norm_weight(w: torch.Tensor, norm_weight: torch.Tensor) -> torch.Tensor:
+    """diag(norm_weight) @ w rounded once to w's dtype (computed in fp32): the
+    weight that takes rms_norm's elementwise scale, so that
+    ``rms_norm(x, g) @ w == diag(rstd(x)) (x @ fold_norm_weight(w, g))`` up to
+    rounding.  Row k of ``w`` (any column layout, e.g. interleaved gate/up) is
+    multiplied by norm_weight[k]."""
+    if w.dim() != 2 or norm_weight.dim() != 1 or norm_weight.numel() != w.size(0):
+        raise ValueError("fold_norm_weight expects w [K, N] and norm_weight [K]")
+    return (w.float() * norm_weight.float().reshape(-1, 1)).to(w.dtype).contiguous()
 
 
 _SCALED_INPUT_DTYPES = (torch.float8_e4m3fn, torch.float8_e5m2, torch.int8)

@@ -39,3 +39,15 @@ def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
     h = torch.empty_like(x)
     torch.ops.aot_kernel.add_rmsnorm_forward(out, h, x, residual, weight, eps)
     return out, h
+
+
+def rms_rstd(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """fp32 rsqrt(mean(x**2, -1) + eps), one value per row: rms_norm's row
+    statistic, for folding the normalisation into the next GEMM
+    (``gemm_silu_mul(x, fold_norm_weight(w_gate_up, w), row_scale=rstd)``)."""
+    if not x.is_cuda:
+        raise ValueError("cuda rms_rstd requires a CUDA tensor")
+    assert_contiguous(x)
+    rstd = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device)
+    torch.ops.aot_kernel.rmsnorm_rstd(rstd, x, eps)
+    return rstd

@@ -13,7 +13,11 @@ slice.  With ``allreduce="fused"`` the down projection and the all-reduce are
 one kernel (``aotk_gemm_allreduce``): partial tiles are summed through
 NVSwitch multicast memory while the rest of the GEMM runs.  A shard built
 with ``fused_silu=True`` (``shard_gate_up_interleaved``) runs the gate/up
-projection and silu(gate) * up as one kernel (``gemm_silu_mul``).
+projection and silu(gate) * up as one kernel (``gemm_silu_mul``); one built
+with ``fold_norm=True`` (``shard_gate_up_folded``) also takes rms_norm into
+that kernel: the norm weight is folded into the rows of the gate/up weight
+once, and each step only computes the row statistic rstd (``rms_rstd``), which
+the GEMM epilogue applies - the normalised activations are never written.
 
 The reference has no multi-GPU code; its oracle for this block is the
 unsharded composition of ref.rmsnorm, ref.gemm and ref.silu.
@@ -29,10 +33,10 @@ import torch.distributed as dist
 
 
 def default_ops() -> SimpleNamespace:
-    from . import gemm, gemm_silu_mul, rms_norm, silu_mul
+    from . import gemm, gemm_silu_mul, rms_norm, rms_rstd, silu_mul
 
     return SimpleNamespace(rms_norm=rms_norm, gemm=gemm, silu_mul=silu_mul,
-                           gemm_silu_mul=gemm_silu_mul)
+                           gemm_silu_mul=gemm_silu_mul, rms_rstd=rms_rstd)
 
 
 def shard_gate_up(w_gate_up: torch.Tensor, rank: int, world: int) -> torch.Tensor:
@@ -53,6 +57,15 @@ def shard_gate_up_interleaved(w_gate_up: torch.Tensor, rank: int, world: int) ->
     shard = shard_gate_up(w_gate_up, rank, world)
     s = shard.shape[1] // 2
     return interleave_gate_up(shard[:, :s], shard[:, s:])
+
+
+def shard_gate_up_folded(w_gate_up: torch.Tensor, norm_weight: torch.Tensor, rank: int,
+                         world: int) -> torch.Tensor:
+    """``shard_gate_up_interleaved`` with the rms_norm weight folded into its
+    rows (``fold_norm_weight``), for ``MLPShard(..., fold_norm=True)``."""
+    from .gemm import fold_norm_weight
+
+    return fold_norm_weight(shard_gate_up_interleaved(w_gate_up, rank, world), norm_weight)
 
 
 def shard_down(w_down: torch.Tensor, rank: int, world: int) -> torch.Tensor:
@@ -125,6 +138,7 @@ class MLPShard:
     w_gate_up: torch.Tensor    # [H, 2*I/W]; interleaved in 128-column blocks when fused_silu
     w_down: torch.Tensor       # [I/W, H]
     fused_silu: bool = False   # w_gate_up is in the gemm_silu_mul layout
+    fold_norm: bool = False    # w_gate_up also carries norm_weight in its rows (needs fused_silu)
 
 
 class TensorParallelMLP:
@@ -142,16 +156,24 @@ class TensorParallelMLP:
         if allreduce not in ("nccl", "fused"):
             raise ValueError(f"allreduce must be 'nccl' or 'fused', got {allreduce!r}")
         self.allreduce = allreduce
+        if shard.fold_norm and not shard.fused_silu:
+            raise ValueError("fold_norm needs the fused gate/up + silu layout (fused_silu=True)")
         self._fused: FusedDownAllReduce | None = None
+
+    def gate_up_act(self, x: torch.Tensor) -> torch.Tensor:
+        """rms_norm, gate/up projection and silu(gate) * up of one step."""
+        ops, s = self.ops, self.shard
+        if s.fold_norm:
+            return ops.gemm_silu_mul(x, s.w_gate_up, ops.rms_rstd(x, self.eps))
+        h = ops.rms_norm(x, s.norm_weight, self.eps)
+        if s.fused_silu:
+            return ops.gemm_silu_mul(h, s.w_gate_up)
+        gu = ops.gemm(h, s.w_gate_up)
+        return ops.silu_mul(gu[:, :self.inter_local], gu[:, self.inter_local:])
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         ops, s = self.ops, self.shard
-        h = ops.rms_norm(x, s.norm_weight, self.eps)
-        if s.fused_silu:
-            act = ops.gemm_silu_mul(h, s.w_gate_up)
-        else:
-            gu = ops.gemm(h, s.w_gate_up)
-            act = ops.silu_mul(gu[:, :self.inter_local], gu[:, self.inter_local:])
+        act = self.gate_up_act(x)
         if self.world == 1:
             return ops.gemm(act, s.w_down)
         if self.allreduce == "fused":

@@ -170,7 +170,21 @@ extern "C" int aotk_gemm_silu_mul(void* act, const void* a, const void* b_gate_u
   using namespace aotk;
   if (I < 0) return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_gemm_silu_mul: negative size");
   if (M == 0 || I == 0) return AOTK_OK;
-  return gemm_silu_mul(act, a, b_gate_up, M, 2 * I, K, dtype, workspace, workspace_bytes, stream);
+  return gemm_silu_mul(act, a, b_gate_up, nullptr, M, 2 * I, K, dtype, workspace, workspace_bytes,
+                       stream);
+}
+
+extern "C" int aotk_gemm_silu_mul_rowscale(void* act, const void* a, const void* b_gate_up,
+                                           const float* row_scale, int64_t M, int64_t I, int64_t K,
+                                           int dtype, void* workspace, size_t workspace_bytes,
+                                           void* stream) {
+  using namespace aotk;
+  if (I < 0) return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_gemm_silu_mul_rowscale: negative size");
+  if (M == 0 || I == 0) return AOTK_OK;
+  if (!row_scale)
+    return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_gemm_silu_mul_rowscale: null row_scale");
+  return gemm_silu_mul(act, a, b_gate_up, row_scale, M, 2 * I, K, dtype, workspace,
+                       workspace_bytes, stream);
 }
 
 namespace aotk {

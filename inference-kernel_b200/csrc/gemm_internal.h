@@ -16,9 +16,12 @@ size_t gemm_tc_workspace_size(int64_t M, int64_t N, int64_t K, int sm_count);
 
 // Persistent tcgen05 GEMM whose epilogue applies silu(gate) * up: b is
 // [K, N2] with gate and up interleaved in blocks of 128 columns, act is
-// [M, N2 / 2] (gemm_tc.cu).  Workspace as for gemm_tc with N = N2.
-int gemm_silu_mul(void* act, const void* a, const void* b, int64_t M, int64_t N2, int64_t K,
-                  int dtype, void* workspace, size_t ws_bytes, void* stream);
+// [M, N2 / 2] (gemm_tc.cu).  With row_scale (fp32 [M], may be null) both
+// accumulators of row m are multiplied by row_scale[m] first.  Workspace as
+// for gemm_tc with N = N2.
+int gemm_silu_mul(void* act, const void* a, const void* b, const float* row_scale, int64_t M,
+                  int64_t N2, int64_t K, int dtype, void* workspace, size_t ws_bytes,
+                  void* stream);
 
 // Persistent tcgen05 GEMM on 8-bit operands (e4m3 or int8, kind::f8f6f4 /
 // kind::i8) with the dequantisation epilogue C = (A * B) * scale_a * scale_b

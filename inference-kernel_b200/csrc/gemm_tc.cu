@@ -727,6 +727,17 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
           }
           const int store_x = nb * kOutCols + (w.half < 0 ? 0 : w.half * (kOutCols / 2)) + c * 64;
           if (store_x >= n_out || store_y >= M) continue;
+          if (sc.sa != nullptr) {
+            // Row scale (an rms_norm rstd folded out of A): gate and up
+            // accumulators are both linear in the row.
+            const int row = mb * kBM + row_in_tile;
+            const float rs = row < M ? __ldg(sc.sa + row) : 0.f;
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+              g[j] *= rs;
+              u[j] *= rs;
+            }
+          }
 #pragma unroll
           for (int j = 0; j < 64; ++j) g[j] = silu_f(g[j]) * u[j];
           store_chunk(g, store_x, store_y);
@@ -997,8 +1008,9 @@ int gemm_tc(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t
                                                                       ws_bytes, s, info);
 }
 
-int gemm_silu_mul(void* act, const void* a, const void* b, int64_t M, int64_t N2, int64_t K,
-                  int dtype, void* workspace, size_t ws_bytes, void* stream) {
+int gemm_silu_mul(void* act, const void* a, const void* b, const float* row_scale, int64_t M,
+                  int64_t N2, int64_t K, int dtype, void* workspace, size_t ws_bytes,
+                  void* stream) {
   DeviceInfo info;
   if (int st = current_device_info(&info)) return st;
   if (int st = require_sm100(info)) return st;
@@ -1009,11 +1021,12 @@ int gemm_silu_mul(void* act, const void* a, const void* b, int64_t M, int64_t N2
                 (long long)N2, kTcBN);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int m = (int)M, n = (int)N2, k = (int)K;
+  const ScaleParams rs{row_scale, nullptr, 1, 0};
   if (dtype == AOTK_BFLOAT16)
     return launch_tc<Op16<__nv_bfloat16>, __nv_bfloat16, kTcBN, kTcStages, kEpiSiluMul>(
-        act, a, b, m, n, k, workspace, ws_bytes, s, info);
-  return launch_tc<Op16<__half>, __half, kTcBN, kTcStages, kEpiSiluMul>(act, a, b, m, n, k,
-                                                                        workspace, ws_bytes, s, info);
+        act, a, b, m, n, k, workspace, ws_bytes, s, info, nullptr, &rs);
+  return launch_tc<Op16<__half>, __half, kTcBN, kTcStages, kEpiSiluMul>(
+      act, a, b, m, n, k, workspace, ws_bytes, s, info, nullptr, &rs);
 }
 
 size_t gemm_scaled_tc_workspace_size(int64_t M, int64_t N, int64_t K, int sm_count) {

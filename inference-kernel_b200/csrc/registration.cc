@@ -127,6 +127,24 @@ void rmsnorm_forward(at::Tensor out, at::Tensor x, at::Tensor weight, double eps
                op);
 }
 
+// rstd[r] = rsqrt(mean(x[r]^2) + eps), fp32, one value per row of x.
+void rmsnorm_rstd(at::Tensor rstd, at::Tensor x, double eps) {
+  const char* op = "rmsnorm_rstd";
+  check_cuda(x, op, "x");
+  check_cuda(rstd, op, "rstd");
+  TORCH_CHECK(x.is_contiguous() && x.dim() >= 1, "[", op, "] x must be contiguous and at least 1-D");
+  TORCH_CHECK(rstd.scalar_type() == at::kFloat && rstd.is_contiguous() && rstd.device() == x.device(),
+              "[", op, "] rstd must be a contiguous float32 tensor on x's device");
+  const int64_t cols = x.dim() >= 1 ? x.size(-1) : 0;
+  const int64_t rows = cols > 0 ? x.numel() / cols : 0;
+  TORCH_CHECK(rstd.numel() == rows, "[", op, "] rstd needs ", rows, " elements, got ", rstd.numel());
+  if (rows == 0) return;
+  c10::cuda::CUDAGuard guard(x.device());
+  check_status(aotk_rmsnorm_rstd(static_cast<float*>(rstd.data_ptr()), x.data_ptr(), rows, cols,
+                                 eps, aotk_dtype(x, op), current_stream(x)),
+               op);
+}
+
 void add_rmsnorm_forward(at::Tensor out, at::Tensor residual_out, at::Tensor x,
                          at::Tensor residual, at::Tensor weight, double eps) {
   const char* op = "add_rmsnorm";
@@ -202,8 +220,8 @@ void gemm_opt(at::Tensor out, at::Tensor a, at::Tensor b) {
                op);
 }
 
-void gemm_silu_mul(at::Tensor out, at::Tensor a, at::Tensor b_gate_up) {
-  const char* op = "gemm_silu_mul";
+void gemm_silu_mul_impl(at::Tensor out, at::Tensor a, at::Tensor b_gate_up,
+                        const at::Tensor* row_scale, const char* op) {
   check_cuda(a, op, "a");
   check_cuda(b_gate_up, op, "b_gate_up");
   check_cuda(out, op, "out");
@@ -219,16 +237,37 @@ void gemm_silu_mul(at::Tensor out, at::Tensor a, at::Tensor b_gate_up) {
               "] tensors must be contiguous");
   const int64_t M = a.size(0), K = a.size(1), I = out.size(1);
   const int dtype = aotk_dtype(a, op);
+  if (row_scale) {
+    TORCH_CHECK(row_scale->scalar_type() == at::kFloat && row_scale->is_contiguous() &&
+                    row_scale->device() == a.device() && row_scale->numel() == M,
+                "[", op, "] row_scale must be a contiguous float32 [M] tensor on a's device");
+  }
   c10::cuda::CUDAGuard guard(a.device());
   size_t ws_bytes = 0;
   check_status(aotk_gemm_silu_mul_workspace_size(M, I, K, dtype, &ws_bytes), op);
   at::Tensor ws;
   if (ws_bytes > 0)
     ws = at::empty({static_cast<int64_t>(ws_bytes)}, a.options().dtype(at::kByte));
-  check_status(aotk_gemm_silu_mul(out.data_ptr(), a.data_ptr(), b_gate_up.data_ptr(), M, I, K, dtype,
-                                  ws_bytes > 0 ? ws.data_ptr() : nullptr, ws_bytes,
-                                  current_stream(a)),
-               op);
+  void* wsp = ws_bytes > 0 ? ws.data_ptr() : nullptr;
+  if (row_scale) {
+    check_status(aotk_gemm_silu_mul_rowscale(out.data_ptr(), a.data_ptr(), b_gate_up.data_ptr(),
+                                             static_cast<const float*>(row_scale->data_ptr()), M,
+                                             I, K, dtype, wsp, ws_bytes, current_stream(a)),
+                 op);
+  } else {
+    check_status(aotk_gemm_silu_mul(out.data_ptr(), a.data_ptr(), b_gate_up.data_ptr(), M, I, K,
+                                    dtype, wsp, ws_bytes, current_stream(a)),
+                 op);
+  }
+}
+
+void gemm_silu_mul(at::Tensor out, at::Tensor a, at::Tensor b_gate_up) {
+  gemm_silu_mul_impl(out, a, b_gate_up, nullptr, "gemm_silu_mul");
+}
+
+void gemm_silu_mul_rowscale(at::Tensor out, at::Tensor a, at::Tensor b_gate_up,
+                            at::Tensor row_scale) {
+  gemm_silu_mul_impl(out, a, b_gate_up, &row_scale, "gemm_silu_mul_rowscale");
 }
 
 // out = (a @ b) * scale_a * scale_b for 8-bit a / b (e4m3, e5m2 or int8);
@@ -323,6 +362,12 @@ TORCH_LIBRARY(aot_kernel, m) {
 
   m.def("gemm_silu_mul(Tensor! out, Tensor a, Tensor b_gate_up) -> ()");
   m.impl("gemm_silu_mul", c10::kCUDA, &gemm_silu_mul);
+
+  m.def("rmsnorm_rstd(Tensor! rstd, Tensor x, float eps) -> ()");
+  m.impl("rmsnorm_rstd", c10::kCUDA, &rmsnorm_rstd);
+
+  m.def("gemm_silu_mul_rowscale(Tensor! out, Tensor a, Tensor b_gate_up, Tensor row_scale) -> ()");
+  m.impl("gemm_silu_mul_rowscale", c10::kCUDA, &gemm_silu_mul_rowscale);
 
   m.def(
       "scaled_gemm(Tensor! out, Tensor a, Tensor b, Tensor scale_a, Tensor scale_b, bool "

@@ -43,11 +43,13 @@ __device__ __forceinline__ void load_row(const T* __restrict__ x, int64_t row, i
 // SM keeps two groups of rows in flight and the grid is a single wave.
 // With kRes, the loaded vectors are x and residual and the row is their
 // rounded sum h, which is also written to h_out.
-template <typename T, int VPT, int TPR, bool kRes>
+// With kStats the kernel writes only the row statistic rstd (fp32, to
+// `stats`) and no normalised row.
+template <typename T, int VPT, int TPR, bool kRes, bool kStats = false>
 __global__ void __launch_bounds__(TPR > kBlock ? TPR : kBlock)
     rmsnorm_vec_kernel(const T* __restrict__ x, const T* __restrict__ res, const T* __restrict__ w,
                        T* __restrict__ y, T* __restrict__ h_out, int64_t rows, int cols,
-                       float eps) {
+                       float eps, float* __restrict__ stats = nullptr) {
   constexpr int E = Elem<T>::kPerVec;
   constexpr int THREADS = TPR > kBlock ? TPR : kBlock;
   constexpr int RPB = THREADS / TPR;  // rows per block
@@ -108,7 +110,9 @@ __global__ void __launch_bounds__(TPR > kBlock ? TPR : kBlock)
       for (int k = 0; k < WPR; ++k) ss += partial[iter & 1][sub][k];
     }
     const float rstd = rsqrtf(ss / (float)cols + eps);
-    if (row < rows) {
+    if constexpr (kStats) {
+      if (row < rows && t == 0) stats[row] = rstd;
+    } else if (row < rows) {
       uint4* yr = reinterpret_cast<uint4*>(y + row * (int64_t)cols);
 #pragma unroll
       for (int i = 0; i < VPT; ++i) {
@@ -172,14 +176,14 @@ __global__ void __launch_bounds__(kBlock) rmsnorm_scalar_kernel(const T* __restr
   }
 }
 
-template <typename T, int VPT, int TPR, bool kRes>
+template <typename T, int VPT, int TPR, bool kRes, bool kStats = false>
 int launch_vec(const T* x, const T* r, const T* w, T* y, T* h, int64_t rows, int cols, float eps,
-               cudaStream_t s) {
+               cudaStream_t s, float* stats = nullptr) {
   constexpr int THREADS = TPR > kBlock ? TPR : kBlock;
   constexpr int RPB = THREADS / TPR;
   DeviceInfo info;
   if (int st = current_device_info(&info)) return st;
-  auto kernel = rmsnorm_vec_kernel<T, VPT, TPR, kRes>;
+  auto kernel = rmsnorm_vec_kernel<T, VPT, TPR, kRes, kStats>;
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, THREADS, 0) != cudaSuccess ||
       per_sm < 1)
@@ -187,7 +191,7 @@ int launch_vec(const T* x, const T* r, const T* w, T* y, T* h, int64_t rows, int
   const int64_t groups = (rows + RPB - 1) / RPB;
   const int64_t capacity = (int64_t)per_sm * info.sm_count;
   const int64_t blocks = groups < capacity ? groups : capacity;
-  kernel<<<(unsigned)blocks, THREADS, 0, s>>>(x, r, w, y, h, rows, cols, eps);
+  kernel<<<(unsigned)blocks, THREADS, 0, s>>>(x, r, w, y, h, rows, cols, eps, stats);
   return check_launch("aotk_rmsnorm_forward");
 }
 
@@ -245,8 +249,94 @@ int dispatch(const void* x, const void* r, const void* w, void* y, void* h, int6
   }
 }
 
+// rstd[row] = rsqrt(mean(x[row]^2) + eps) in fp32 and nothing else: the row
+// statistic of rms_norm for callers that fold the normalisation into a GEMM
+// (x @ (diag(w) W) scaled by rstd per row, aotk_gemm_silu_mul_rowscale).
+// Long rows take rmsnorm_vec_kernel in statistics-only mode; this kernel
+// serves short and unaligned rows: one warp per row, 16-byte loads, 8 in
+// flight per lane; x is read once.
+template <typename T, bool kVec>
+__global__ void __launch_bounds__(kBlock) rms_rstd_kernel(const T* __restrict__ x,
+                                                          float* __restrict__ rstd, int64_t rows,
+                                                          int64_t cols, float eps) {
+  constexpr int E = Elem<T>::kPerVec;
+  const int64_t row = (int64_t)blockIdx.x * (kBlock / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float ss = 0.0f;
+  if constexpr (kVec) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + row * cols);
+    const int64_t n_vec = cols / E;
+    for (int64_t v0 = lane; v0 < n_vec; v0 += 8 * 32) {
+      uint4 v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int64_t idx = v0 + i * 32;
+        v[i] = idx < n_vec ? ld_stream(xr + idx) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float f[E];
+        Elem<T>::unpack(v[i], f);
+#pragma unroll
+        for (int e = 0; e < E; ++e) ss = fmaf(f[e], f[e], ss);
+      }
+    }
+  } else {
+    for (int64_t c = lane; c < cols; c += 32) {
+      const float f = Elem<T>::to_f(x[row * cols + c]);
+      ss = fmaf(f, f, ss);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) rstd[row] = rsqrtf(ss / (float)cols + eps);
+}
+
+template <typename T>
+int launch_rstd(const void* xv, float* rstd, int64_t rows, int64_t cols, float eps,
+                cudaStream_t s) {
+  const T* x = static_cast<const T*>(xv);
+  constexpr int E = Elem<T>::kPerVec;
+  const int64_t n_vec = cols / E;
+  // Rows that fit the persistent vector kernel use it in statistics-only
+  // mode (the same row layout and prefetch as rms_norm, no output row).
+  if (cols % E == 0 && aligned16(x) && n_vec <= 8 * 1024 && n_vec > 128) {
+    const int nv = (int)n_vec, c = (int)cols;
+    if (nv <= 8 * 32) return launch_vec<T, 8, 32, false, true>(x, nullptr, nullptr, nullptr, nullptr, rows, c, eps, s, rstd);
+    if (nv <= 8 * 64) return launch_vec<T, 8, 64, false, true>(x, nullptr, nullptr, nullptr, nullptr, rows, c, eps, s, rstd);
+    if (nv <= 8 * 128) return launch_vec<T, 8, 128, false, true>(x, nullptr, nullptr, nullptr, nullptr, rows, c, eps, s, rstd);
+    if (nv <= 8 * 256) return launch_vec<T, 8, 256, false, true>(x, nullptr, nullptr, nullptr, nullptr, rows, c, eps, s, rstd);
+    if (nv <= 8 * 512) return launch_vec<T, 8, 512, false, true>(x, nullptr, nullptr, nullptr, nullptr, rows, c, eps, s, rstd);
+    return launch_vec<T, 8, 1024, false, true>(x, nullptr, nullptr, nullptr, nullptr, rows, c, eps, s, rstd);
+  }
+  const int64_t blocks = (rows + kBlock / 32 - 1) / (kBlock / 32);
+  if (blocks > 0x7fffffffLL) return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_rmsnorm_rstd: too many rows");
+  if (cols % E == 0 && aligned16(x))
+    rms_rstd_kernel<T, true><<<(unsigned)blocks, kBlock, 0, s>>>(x, rstd, rows, cols, eps);
+  else
+    rms_rstd_kernel<T, false><<<(unsigned)blocks, kBlock, 0, s>>>(x, rstd, rows, cols, eps);
+  return check_launch("aotk_rmsnorm_rstd");
+}
+
 }  // namespace
 }  // namespace aotk
+
+extern "C" int aotk_rmsnorm_rstd(float* rstd, const void* x, int64_t rows, int64_t cols, double eps,
+                                 int dtype, void* stream) {
+  using namespace aotk;
+  if (rows < 0 || cols < 0) return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_rmsnorm_rstd: negative size");
+  if (rows == 0) return AOTK_OK;
+  if (!rstd || (cols > 0 && !x)) return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_rmsnorm_rstd: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const float e = static_cast<float>(eps);
+  switch (dtype) {
+    case AOTK_FLOAT32: return launch_rstd<float>(x, rstd, rows, cols, e, s);
+    case AOTK_FLOAT16: return launch_rstd<__half>(x, rstd, rows, cols, e, s);
+    case AOTK_BFLOAT16: return launch_rstd<__nv_bfloat16>(x, rstd, rows, cols, e, s);
+    default: return fail(AOTK_ERR_UNSUPPORTED, "aotk_rmsnorm_rstd: unsupported dtype %d", dtype);
+  }
+}
 
 extern "C" int aotk_rmsnorm_forward(void* out, const void* x, const void* weight, int64_t rows,
                                     int64_t cols, double eps, int dtype, void* stream) {

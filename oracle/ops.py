@@ -121,6 +121,32 @@ def gemm_silu_mul(a: np.ndarray, w_gate: np.ndarray, w_up: np.ndarray, dtype: st
     return round_to(_silu_f32(g) * u, dtype)
 
 
+def rms_rstd(x: np.ndarray, eps: float) -> np.ndarray:
+    """rms_norm's row statistic rsqrt(mean(x^2) + eps) in fp32 (the factor
+    ``rmsnorm`` applies before the weight)."""
+    x = np.asarray(x, dtype=np.float32)
+    ms = np.mean(x * x, axis=-1, dtype=np.float32)
+    return (np.float32(1.0) / np.sqrt(ms + np.float32(eps))).astype(np.float32)
+
+
+def gemm_silu_mul_folded(x: np.ndarray, norm_w: np.ndarray, w_gate: np.ndarray,
+                         w_up: np.ndarray, eps: float, dtype: str) -> np.ndarray:
+    """rms_norm folded into the fused gate/up kernel: the norm weight scales
+    the weight rows once (W' = diag(w) W rounded to `dtype`), the GEMM runs
+    on x, and each row's fp32 accumulators are multiplied by rstd before
+    silu(gate) * up and the single rounding.  Equal to
+    ``gemm_silu_mul(rmsnorm(x, w), W_gate, W_up)`` up to where the roundings
+    fall."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.asarray(norm_w, dtype=np.float32).reshape(-1, 1)
+    wg = round_to(np.asarray(w_gate, dtype=np.float32) * w, dtype)
+    wu = round_to(np.asarray(w_up, dtype=np.float32) * w, dtype)
+    rstd = rms_rstd(x, eps).reshape(-1, 1)
+    g = (x @ wg) * rstd
+    u = (x @ wu) * rstd
+    return round_to(_silu_f32(g) * u, dtype)
+
+
 def mlp_block(x, norm_w, w_gate_up, w_down, eps: float, dtype: str) -> np.ndarray:
     """Unsharded Llama MLP block as a composition of the ops above:
     rms_norm -> x @ [W_gate | W_up] -> silu(gate) * up -> @ W_down.

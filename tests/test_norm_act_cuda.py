@@ -208,3 +208,44 @@ def test_silu_and_silu_mul_config_size():
     rows = slice(0, 8192, 97)
     assert_close_common(s[rows], ops.silu(g[rows], "bfloat16"), "bfloat16")
     assert_close_common(sm[rows], ops.silu_mul(g[rows], u[rows], "bfloat16"), "bfloat16")
+
+
+# ---- rms_norm's row statistic and rms_norm folded into the gate/up GEMM ----
+
+@pytest.mark.parametrize("shape", [(4096, 8192), (7, 1000), (3, 4096), (1, 70000)], ids=str)
+def test_rms_rstd_matches_oracle(shape):
+    import aot_kernel
+
+    x = randn(shape, sum(shape), "bfloat16")
+    got = aot_kernel.rms_rstd(to_device(x, "bfloat16"), 1e-6).cpu().numpy()
+    want = ops.rms_rstd(x, 1e-6)
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=0)  # fp32 sums in another order
+
+
+@pytest.mark.parametrize("shape", [(256, 512, 256), (300, 1024, 384), (2048, 4096, 1792)], ids=str)
+def test_gemm_silu_mul_folded_norm_matches_oracle(shape):
+    """(M, H, I): rms_rstd(x) + gemm_silu_mul(x, fold_norm_weight(W), row_scale)
+    against the folded oracle, and against the unfused rms_norm -> gate/up ->
+    silu_mul composition within the GEMM tolerance."""
+    import torch
+
+    import aot_kernel
+    from tests.conftest import assert_close_for_gemm
+
+    M, H, inter = shape
+    x = randn((M, H), M + 11, "bfloat16")
+    nw = randn((H,), H + 12, "bfloat16", mean=1.0, std=0.1)
+    wg = randn((H, inter), H + 13, "bfloat16", std=H ** -0.5)
+    wu = randn((H, inter), H + 14, "bfloat16", std=H ** -0.5)
+    tx = to_device(x, "bfloat16")
+    w = aot_kernel.interleave_gate_up(to_device(wg, "bfloat16"), to_device(wu, "bfloat16"))
+    wf = aot_kernel.fold_norm_weight(w, to_device(nw, "bfloat16"))
+    act = aot_kernel.gemm_silu_mul(tx, wf, aot_kernel.rms_rstd(tx, 1e-6))
+    torch.cuda.synchronize()
+    rows = np.unique(np.concatenate([np.random.default_rng(4).integers(0, M, size=40),
+                                     np.arange(max(0, M - 128), M, 7)]))
+    got = act[torch.as_tensor(rows, device="cuda")]
+    assert_close_for_gemm(got, ops.gemm_silu_mul_folded(x[rows], nw, wg, wu, 1e-6, "bfloat16"),
+                          "bfloat16")
+    unfused = ops.gemm_silu_mul(ops.rmsnorm(x[rows], nw, 1e-6, "bfloat16"), wg, wu, "bfloat16")
+    assert_close_for_gemm(got, unfused, "bfloat16")

@@ -49,17 +49,24 @@ def _rank_main(rank: int, world: int, port: int, chunks: int, out_dir: str,
     import torch.distributed as dist
 
     from aot_kernel.tp_mlp import (MLPShard, TensorParallelMLP, shard_down, shard_gate_up,
-                                   shard_gate_up_interleaved)
+                                   shard_gate_up_folded, shard_gate_up_interleaved)
 
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
                             device_id=dev)
     x, nw, wgu, wd = (torch.from_numpy(a).to(dev, torch.bfloat16) for a in _weights())
-    fused_silu = allreduce == "fused"  # the fused runs also take the fused gate/up + silu path
-    wgu_r = (shard_gate_up_interleaved if fused_silu else shard_gate_up)(wgu, rank, world)
-    block = TensorParallelMLP(MLPShard(nw, wgu_r, shard_down(wd, rank, world), fused_silu=fused_silu),
-                              chunks=chunks, allreduce=allreduce)
+    # The fused runs also take the fused gate/up + silu path; "fused_fold"
+    # additionally folds rms_norm into it.
+    fused_silu = allreduce.startswith("fused")
+    fold = allreduce == "fused_fold"
+    if fold:
+        wgu_r = shard_gate_up_folded(wgu, nw, rank, world)
+    else:
+        wgu_r = (shard_gate_up_interleaved if fused_silu else shard_gate_up)(wgu, rank, world)
+    block = TensorParallelMLP(MLPShard(nw, wgu_r, shard_down(wd, rank, world), fused_silu=fused_silu,
+                                       fold_norm=fold),
+                              chunks=chunks, allreduce="fused" if fused_silu else allreduce)
     y = block(x)
     y = block(x).clone()  # second call: epoch 2 of the fused path
     torch.cuda.synchronize()
@@ -80,23 +87,28 @@ def _check(y: np.ndarray, world: int) -> None:
     assert err <= 2e-2 * np.abs(full).max(), f"W={world}: max|err| {err} vs max|ref| {np.abs(full).max()}"
 
 
-@pytest.mark.parametrize("fused_silu", [False, True])
-def test_block_single_gpu(fused_silu):
+@pytest.mark.parametrize("mode", ["unfused", "fused_silu", "fold_norm"])
+def test_block_single_gpu(mode):
     import torch
 
-    from aot_kernel.tp_mlp import MLPShard, TensorParallelMLP, shard_gate_up_interleaved
+    from aot_kernel.tp_mlp import (MLPShard, TensorParallelMLP, shard_gate_up_folded,
+                                   shard_gate_up_interleaved)
 
     x, nw, wgu, wd = (torch.from_numpy(a).to("cuda", torch.bfloat16) for a in _weights())
-    if fused_silu:
+    if mode == "fused_silu":
         wgu = shard_gate_up_interleaved(wgu, 0, 1)
-    y = TensorParallelMLP(MLPShard(nw, wgu, wd, fused_silu=fused_silu))(x)
+    elif mode == "fold_norm":
+        wgu = shard_gate_up_folded(wgu, nw, 0, 1)
+    y = TensorParallelMLP(MLPShard(nw, wgu, wd, fused_silu=mode != "unfused",
+                                   fold_norm=mode == "fold_norm"))(x)
     torch.cuda.synchronize()
     _check(y.float().cpu().numpy(), 1)
 
 
 @pytest.mark.parametrize("world,chunks,allreduce",
                          [(2, 1, "nccl"), (2, 4, "nccl"), (4, 1, "nccl"), (8, 2, "nccl"),
-                          (2, 1, "fused"), (4, 1, "fused"), (8, 1, "fused")])
+                          (2, 1, "fused"), (4, 1, "fused"), (8, 1, "fused"), (2, 1, "fused_fold"),
+                          (8, 1, "fused_fold")])
 def test_block_tensor_parallel(world, chunks, allreduce, tmp_path):
     if _gpu_count() < world:
         pytest.skip(f"needs {world} GPUs")
