@@ -455,6 +455,8 @@ def kernel_table(peaks: dict) -> dict:
     xs = [rand_bf16((rows, cols), 20 + 2 * i) for i in range(R)]
     out["rms_norm_8192x4096"] = hbm_entry([lambda x=x: aot_kernel.rms_norm(x, w) for x in xs],
                                           2.0 * rows * cols * 2 + cols * 2, R)
+    out["rms_rstd_8192x4096"] = hbm_entry([lambda x=x: aot_kernel.rms_rstd(x) for x in xs],
+                                          1.0 * rows * cols * 2 + rows * 4, R)
     rs = [rand_bf16((rows, cols), 40 + 2 * i) for i in range(R)]
     out["add_rms_norm_8192x4096"] = hbm_entry(
         [lambda x=x, r=r: aot_kernel.add_rmsnorm(x, r, w) for x, r in zip(xs, rs)],
