@@ -87,8 +87,6 @@ int64_t block_rows(int64_t M) {
       return fail(AOTK_ERR_CUDA, "aotk_gemm_host: %s: %s", #expr, cudaGetErrorString(e_));    \
   } while (0)
 
-}  // namespace
-
 int gemm_host(void* c_host, const void* a_host, const void* b_host, int64_t M, int64_t N,
               int64_t K, int dtype, void* a_dev, void* b_dev, void* c_dev, void* workspace,
               size_t workspace_bytes, void* stream_v) {
@@ -145,6 +143,7 @@ int gemm_host(void* c_host, const void* a_host, const void* b_host, int64_t M, i
   return AOTK_OK;
 }
 
+}  // namespace
 }  // namespace aotk
 
 extern "C" int aotk_gemm_host_workspace_size(int64_t M, int64_t N, int64_t K, int dtype,
