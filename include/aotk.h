@@ -315,6 +315,16 @@ AOTK_API int aotk_gemm_allreduce_tiles(int64_t M, int64_t N, int64_t* tiles);
 AOTK_API int aotk_gemm_allreduce(const void* a, const void* b, int64_t M, int64_t N, int64_t K,
                                  int dtype, const aotk_allreduce_buffers* bufs, void* stream);
 
+/* The persistent tcgen05 kernel's tile schedule for an [M, N, K] problem of
+ * elem_bytes-byte operands (2: fp16/bf16, 1: the scaled 8-bit GEMM) on a
+ * device with sm_count SMs, with or without a K-split workspace; pure host
+ * arithmetic, no device access.  out[10] receives: grid, tiles (128 x 256),
+ * whole-tile rounds, first tail tile, halves (1: tail tiles run as two
+ * 128 x 128 halves), K splits per tail tile, K blocks per split, tail work
+ * items, K blocks, workspace bytes needed.  For tests and capacity planning. */
+AOTK_API int aotk_gemm_schedule(int64_t M, int64_t N, int64_t K, int elem_bytes, int sm_count,
+                                int with_workspace, int64_t* out);
+
 /* Watchdog word of the tcgen05 kernels on `device`: a bit mask of pipeline
  * waits that gave up after their time limit (0 = healthy).  Synchronises the
  * device.  clear != 0 resets it to 0 after reading. */

@@ -47,6 +47,7 @@ SIGNATURES: dict[str, list] = {
     "aotk_gemm_silu_mul": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr, ctypes.c_size_t, _ptr],
     "aotk_gemm_silu_mul_workspace_size": [_i64, _i64, _i64, _int, ctypes.POINTER(ctypes.c_size_t)],
     "aotk_gemm_allreduce": [_ptr, _ptr, _i64, _i64, _i64, _int, ctypes.c_void_p, _ptr],
+    "aotk_gemm_schedule": [_i64, _i64, _i64, _int, _int, _int, ctypes.POINTER(ctypes.c_int64)],
     "aotk_rmsnorm_rstd": [_ptr, _ptr, _i64, _i64, ctypes.c_double, _int, _ptr],
     "aotk_gemm_silu_mul_rowscale": [_ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr,
                                     ctypes.c_size_t, _ptr],
@@ -223,6 +224,17 @@ def gemm_silu_mul(act, a, b_gate_up, M, I, K, dtype, workspace=None, workspace_b
                   stream=None) -> None:
     _call("aotk_gemm_silu_mul", _p(act), _p(a), _p(b_gate_up), M, I, K, dtype, _p(workspace),
           workspace_bytes, _stream(stream))
+
+
+SCHEDULE_FIELDS = ("grid", "tiles", "full_rounds", "split_begin", "halves", "splits",
+                   "kb_per_split", "units", "kblocks", "ws_bytes")
+
+
+def gemm_schedule(M: int, N: int, K: int, elem_bytes: int, sm_count: int,
+                  with_workspace: bool) -> dict:
+    out = (ctypes.c_int64 * len(SCHEDULE_FIELDS))()
+    _call("aotk_gemm_schedule", M, N, K, elem_bytes, sm_count, int(with_workspace), out)
+    return dict(zip(SCHEDULE_FIELDS, list(out)))
 
 
 def rmsnorm_rstd(rstd, x, rows: int, cols: int, eps: float, dtype: int, stream=None) -> None:

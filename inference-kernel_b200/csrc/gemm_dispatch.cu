@@ -289,6 +289,13 @@ extern "C" int aotk_scaled_gemm(void* c, const void* a, const void* b, const flo
                           stream);
 }
 
+extern "C" int aotk_gemm_schedule(int64_t M, int64_t N, int64_t K, int elem_bytes, int sm_count,
+                                  int with_workspace, int64_t* out) {
+  using namespace aotk;
+  if (!out) return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_gemm_schedule: null pointer");
+  return gemm_tc_schedule(M, N, K, elem_bytes, sm_count, with_workspace != 0, out);
+}
+
 extern "C" int aotk_gemm_allreduce_tiles(int64_t M, int64_t N, int64_t* tiles) {
   using namespace aotk;
   if (!tiles || M < 0 || N < 0)

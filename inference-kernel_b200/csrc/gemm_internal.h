@@ -23,6 +23,13 @@ int gemm_silu_mul(void* act, const void* a, const void* b, const float* row_scal
                   int64_t N2, int64_t K, int dtype, void* workspace, size_t ws_bytes,
                   void* stream);
 
+// The persistent kernel's schedule for a problem on `sm_count` SMs (no device
+// access): out[0..9] = grid, tiles, whole-tile rounds, first tail tile,
+// halves, K splits, K blocks per split, tail work items, K blocks, workspace
+// bytes (gemm_tc.cu).
+int gemm_tc_schedule(int64_t M, int64_t N, int64_t K, int elem_bytes, int sm_count,
+                     bool with_workspace, int64_t* out);
+
 // Persistent tcgen05 GEMM on 8-bit operands (e4m3 or int8, kind::f8f6f4 /
 // kind::i8) with the dequantisation epilogue C = (A * B) * scale_a * scale_b
 // (gemm_tc.cu).  The caller has checked shapes, alignment and dtypes

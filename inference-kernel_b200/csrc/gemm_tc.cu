@@ -1070,6 +1070,27 @@ int gemm_scaled_tc(void* c, const void* a, const void* b, const float* scale_a,
   return launch_scaled<OpS8>(c, a, b, m, n, k, out_dtype, sc, workspace, ws_bytes, s, info);
 }
 
+int gemm_tc_schedule(int64_t M, int64_t N, int64_t K, int elem_bytes, int sm_count,
+                     bool with_workspace, int64_t* out) {
+  if (M <= 0 || N <= 0 || K <= 0 || M >= (1LL << 31) || N >= (1LL << 31) || K >= (1LL << 31) ||
+      (elem_bytes != 1 && elem_bytes != 2) || sm_count <= 0)
+    return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_gemm_schedule: bad arguments");
+  const int bk = elem_bytes == 1 ? OpShape<1>::kBK : OpShape<2>::kBK;
+  const TcPlan p = plan_tc((int)M, (int)N, (int)K, kTcBN, bk, sm_count, with_workspace, true);
+  const TcSched& s = p.sched;
+  out[0] = p.grid;
+  out[1] = s.num_tiles;
+  out[2] = s.full_rounds;
+  out[3] = s.split_begin;
+  out[4] = s.halves;
+  out[5] = s.splits;
+  out[6] = s.kb_per_split;
+  out[7] = s.units;
+  out[8] = s.kblocks;
+  out[9] = static_cast<int64_t>(p.ws_bytes);
+  return AOTK_OK;
+}
+
 int gemm_allreduce_tiles(int64_t M, int64_t N) {
   return static_cast<int>(((M + kBM - 1) / kBM) * ((N + kTcBN - 1) / kTcBN));
 }
