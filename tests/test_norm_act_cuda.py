@@ -222,11 +222,14 @@ def test_rms_rstd_matches_oracle(shape):
     np.testing.assert_allclose(got, want, rtol=1e-5, atol=0)  # fp32 sums in another order
 
 
-@pytest.mark.parametrize("shape", [(256, 512, 256), (300, 1024, 384), (2048, 4096, 1792)], ids=str)
+@pytest.mark.parametrize("shape", [(256, 512, 256), (300, 1024, 384), (2048, 4096, 1792),
+                                   (4096, 8192, 3584)], ids=str)
 def test_gemm_silu_mul_folded_norm_matches_oracle(shape):
     """(M, H, I): rms_rstd(x) + gemm_silu_mul(x, fold_norm_weight(W), row_scale)
     against the folded oracle, and against the unfused rms_norm -> gate/up ->
-    silu_mul composition within the GEMM tolerance."""
+    silu_mul composition within the GEMM tolerance.  The last shape is the
+    8-way tensor-parallel gate/up of the Llama-70B block (896 tiles: 8 left
+    over, cut along K through the workspace, then row-scaled)."""
     import torch
 
     import aot_kernel

@@ -217,6 +217,8 @@ TC_SHAPES = [
     (200, 384, 272),      # ragged M and N inside the tiles (N % 16 == 0)
     (1, 512, 1024),       # decode row
     (1024, 1024, 1024),
+    (64, 16, 32),         # one K step of 16 bytes, N narrower than a box
+    (2304, 256, 4096),    # 288 tiles: one wave and 140 left, run whole
 ]
 
 
