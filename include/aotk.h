@@ -326,7 +326,10 @@ AOTK_API int aotk_gemm_schedule(int64_t M, int64_t N, int64_t K, int elem_bytes,
                                 int with_workspace, int64_t* out);
 
 /* Watchdog word of the tcgen05 kernels on `device`: a bit mask of pipeline
- * waits that gave up after their time limit (0 = healthy).  Synchronises the
+ * waits that gave up after their time limit (0 = healthy).  Persistent
+ * kernel: 1 producer, 2 MMA, 4 epilogue, 64 peer / flag wait, 128 self-test,
+ * 2048 K-split partials; skinny kernel: 8, 16, 32; CTA-pair kernel: 256,
+ * 512, 1024.  Synchronises the
  * device.  clear != 0 resets it to 0 after reading. */
 AOTK_API int aotk_watchdog_status(int device, uint32_t* status, int clear);
 

@@ -60,11 +60,13 @@ constexpr int kMaxSplits = 4;
 // K blocks it cut the kernel time by 13 %).
 constexpr int kSplitMinKblocks = 128;
 
+// Watchdog bits of this kernel (the skinny kernel uses 8-32, the CTA-pair
+// kernel 256-1024; aotk_watchdog_status ORs all of them).
 enum : unsigned {
   kWdProducer = 1u,
   kWdMma = 2u,
   kWdEpilogue = 4u,
-  kWdSplit = 8u,  // the last K-split unit gave up waiting for the other partials
+  kWdSplit = 2048u,  // the last K-split unit gave up waiting for the other partials
   kWdPeer = 64u,
   kWdSelfTest = 128u
 };
