@@ -309,7 +309,7 @@ def test_split_and_whole_schedules_agree():
 # ---- gate/up GEMM fused with silu(gate) * up ----
 
 @pytest.mark.parametrize("shape", [(256, 512, 256), (300, 328, 384), (2560, 1024, 1024),
-                                   (4096, 8192, 3584)], ids=str)
+                                   (4096, 8192, 3584), (2048, 4096, 3072)], ids=str)
 def test_gemm_silu_mul_matches_oracle(shape):
     """(M, K, I): interleaved [K, 2I] weight, act [M, I]; the tails of the
     first three run as N halves (each half keeps matching gate and up
