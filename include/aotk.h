@@ -160,7 +160,8 @@ AOTK_API int aotk_gemm_opt_noalloc(void* c, const void* a, const void* b, int64_
 /* aotk_gemm_opt on host-resident operands: c_host[M, N] = a_host[M, K] *
  * b_host[K, N], FLOAT16 / BFLOAT16, through caller-provided device buffers
  * a_dev [M, K], b_dev [K, N], c_dev [M, N] of the same dtype.  B is copied in
- * first, then A in blocks of 128-row multiples (about eight); the GEMM of
+ * first, then A in blocks of 128-row multiples (about M/8, the last eighth
+ * in four smaller blocks to shorten the tail); the GEMM of
  * block i runs on `stream` as soon as its rows have landed while the next
  * block is still in flight, and block i of C is copied out while later blocks
  * compute, so inbound copies, GEMMs and outbound copies overlap.  Host
