@@ -4,11 +4,13 @@
 // element for silu/relu, 4 + 2 for silu_mul).  Each thread moves 16-byte
 // vectors, issues all UNROLL loads of an iteration before any math so that
 // UNROLL * 16 bytes per thread are in flight, and walks the tensor with a
-// grid-stride loop over a grid sized to the SM count.  The reference runs one
+// grid-stride loop over a grid of exactly one wave of resident blocks.  The reference runs one
 // scalar element per thread with 458 752 blocks at [8192, 14336]
 // (aot_kernel/csrc/activation/silu.cu:14-19, :29-39).
 #include "common.h"
 #include "vec.cuh"
+
+#include <mutex>
 
 namespace aotk {
 namespace {
@@ -117,9 +119,32 @@ __global__ void __launch_bounds__(kThreads) silu_mul_scalar_kernel(
   }
 }
 
-int grid_for(int64_t work_items, int per_block, const DeviceInfo& info) {
+// Blocks of `kernel` that are resident at once on one SM of the current
+// device (cached per kernel and device; at most kBlocksPerSm).
+int resident_per_sm(const void* kernel, const DeviceInfo& info) {
+  struct Entry {
+    const void* kernel;
+    int device, n;
+  };
+  static std::mutex mu;
+  static Entry cache[64];
+  static int count = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < count; ++i)
+    if (cache[i].kernel == kernel && cache[i].device == info.device) return cache[i].n;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kThreads, 0) != cudaSuccess || n < 1)
+    n = 1;
+  if (n > kBlocksPerSm) n = kBlocksPerSm;
+  if (count < 64) cache[count++] = Entry{kernel, info.device, n};
+  return n;
+}
+
+// Grid of the grid-stride kernels: one wave of resident blocks (a grid
+// larger than what fits would run its last blocks as a partial second wave).
+int grid_for(const void* kernel, int64_t work_items, int per_block, const DeviceInfo& info) {
   const int64_t want = (work_items + per_block - 1) / per_block;
-  const int64_t cap = (int64_t)info.sm_count * kBlocksPerSm;
+  const int64_t cap = (int64_t)info.sm_count * resident_per_sm(kernel, info);
   return (int)(want < cap ? (want > 0 ? want : 1) : cap);
 }
 
@@ -132,16 +157,19 @@ int launch_unary(void* out, const void* x, int64_t n, cudaStream_t stream, const
   if (aligned16(out) && aligned16(x)) {
     const int64_t n_vec = n / E;
     if (n_vec > 0) {
-      unary_vec_kernel<T, Op><<<grid_for(n_vec, kThreads * kUnroll, info), kThreads, 0, stream>>>(
-          static_cast<const uint4*>(x), static_cast<uint4*>(out), n_vec);
+      auto kernel = unary_vec_kernel<T, Op>;
+      kernel<<<grid_for(reinterpret_cast<const void*>(kernel), n_vec, kThreads * kUnroll, info),
+               kThreads, 0, stream>>>(static_cast<const uint4*>(x), static_cast<uint4*>(out),
+                                      n_vec);
       if (int st = check_launch(name)) return st;
     }
     head = n_vec * E;
   }
   const int64_t tail = n - head;
   if (tail > 0) {
-    unary_scalar_kernel<T, Op><<<grid_for(tail, kThreads, info), kThreads, 0, stream>>>(
-        static_cast<const T*>(x) + head, static_cast<T*>(out) + head, tail);
+    auto kernel = unary_scalar_kernel<T, Op>;
+    kernel<<<grid_for(reinterpret_cast<const void*>(kernel), tail, kThreads, info), kThreads, 0,
+             stream>>>(static_cast<const T*>(x) + head, static_cast<T*>(out) + head, tail);
     if (int st = check_launch(name)) return st;
   }
   return AOTK_OK;
@@ -172,13 +200,16 @@ int launch_silu_mul(void* out, int64_t out_stride, const void* gate, int64_t gat
                       out_stride % E == 0 && gate_stride % E == 0 && up_stride % E == 0;
   if (vec_ok) {
     const int64_t vpr = cols / E;
-    silu_mul_vec_kernel<T><<<grid_for(rows * vpr, kThreads * kUnroll, info), kThreads, 0, stream>>>(
-        static_cast<const T*>(gate), gate_stride, static_cast<const T*>(up), up_stride,
-        static_cast<T*>(out), out_stride, rows, vpr);
+    auto kernel = silu_mul_vec_kernel<T>;
+    kernel<<<grid_for(reinterpret_cast<const void*>(kernel), rows * vpr, kThreads * kUnroll, info),
+             kThreads, 0, stream>>>(static_cast<const T*>(gate), gate_stride,
+                                    static_cast<const T*>(up), up_stride, static_cast<T*>(out),
+                                    out_stride, rows, vpr);
   } else {
-    silu_mul_scalar_kernel<T><<<grid_for(rows * cols, kThreads, info), kThreads, 0, stream>>>(
-        static_cast<const T*>(gate), gate_stride, static_cast<const T*>(up), up_stride,
-        static_cast<T*>(out), out_stride, rows, cols);
+    auto kernel = silu_mul_scalar_kernel<T>;
+    kernel<<<grid_for(reinterpret_cast<const void*>(kernel), rows * cols, kThreads, info), kThreads,
+             0, stream>>>(static_cast<const T*>(gate), gate_stride, static_cast<const T*>(up),
+                          up_stride, static_cast<T*>(out), out_stride, rows, cols);
   }
   return check_launch("aotk_silu_mul_forward");
 }
