@@ -11,7 +11,8 @@
 // speed plus one block's GEMM and copy-out.
 //
 // Two copy streams per device (inbound, outbound) and a pool of events are
-// created on first use and kept; the GEMM blocks run on the caller's stream,
+// created on first use and kept (calls on one device are serialised while
+// they enqueue, see gemm_host); the GEMM blocks run on the caller's stream,
 // which at return is ordered after the last copy-out, so the call behaves as
 // one stream-ordered operation.  Host buffers should be page-locked
 // (cudaHostAlloc / cudaHostRegister) for the copies to overlap.
@@ -36,6 +37,7 @@ constexpr int kMaxBlocks = 16;
 constexpr int kRowAlign = 128;  // the tcgen05 tile height
 
 struct HostPipe {
+  std::mutex mu;  // one call's enqueue sequence at a time (the events are shared)
   cudaStream_t in = nullptr, out = nullptr;
   cudaEvent_t start = nullptr, end = nullptr;
   cudaEvent_t a_ready[kMaxBlocks] = {};
@@ -117,6 +119,11 @@ int gemm_host(void* c_host, const void* a_host, const void* b_host, int64_t M, i
   AOTK_HOST_CHECK(cudaGetDevice(&device));
   HostPipe* p = nullptr;
   if (int st = pipe_for(device, &p)) return st;
+  // Calls from several host threads enqueue one after another: each call's
+  // event records and the waits on them are issued together, so a wait never
+  // picks up another call's record.  The copies of calls on one device share
+  // the two copy streams and therefore run in call order.
+  std::lock_guard<std::mutex> lock(p->mu);
   cudaStream_t s = static_cast<cudaStream_t>(stream_v);
   const size_t es = 2;
   int64_t rows[kMaxBlocks];
