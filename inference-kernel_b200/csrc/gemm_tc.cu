@@ -409,6 +409,10 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
   const int tiles_n = sched.tiles_n;
   volatile int* last_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 8);
 
+  // Programmatic dependent launch: the next kernel on the stream may start
+  // its own prologue as SMs free up; this one touches global memory only
+  // after pdl_wait_prior() below, once the previous kernel has completed.
+  pdl_launch_dependents();
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -433,6 +437,7 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait_prior();
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -979,8 +984,23 @@ int launch_tc(void* c, const void* a, const void* b, int M, int N, int K, void* 
   if (ar) arp = *ar;
   ScaleParams scp{};
   if (scales) scp = *scales;
-  kernel<<<p.grid, kFused ? kThreadsFused : kThreads, L::kAlloc, stream>>>(
-      ta, tb, tc, static_cast<T*>(c), M, N, K, idesc, p.sched, arp, scp);
+  // Launched with programmatic stream serialisation (see the kernel's
+  // prologue): barrier set-up, TMEM allocation and descriptor prefetch
+  // overlap the tail of the previous kernel.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.grid), 1, 1);
+  cfg.blockDim = dim3(kFused ? kThreadsFused : kThreads, 1, 1);
+  cfg.dynamicSmemBytes = L::kAlloc;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, static_cast<T*>(c), M, N, K, idesc,
+                                     p.sched, arp, scp);
+  if (e != cudaSuccess)
+    return fail(AOTK_ERR_CUDA, "tcgen05 gemm launch (grid %d): %s", p.grid, cudaGetErrorString(e));
   return check_launch("tcgen05 gemm");
 }
 
