@@ -28,13 +28,16 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _weights():
+def _weights(mode: str = "plain"):
+    """Block weights; the fused layouts need 128-column blocks per rank, so
+    their intermediate size is 512 (4 ranks x 128)."""
     from oracle.inputs import randn
 
+    inter = INTER if mode == "plain" else 512
     x = randn((T, H), SEEDS[0])
     nw = randn((H,), SEEDS[1], mean=1.0, std=0.1)
-    wgu = randn((H, 2 * INTER), SEEDS[2], std=0.15)
-    wd = randn((INTER, H), SEEDS[3], std=0.15)
+    wgu = randn((H, 2 * inter), SEEDS[2], std=0.15)
+    wd = randn((inter, H), SEEDS[3], std=0.15 * (INTER / inter) ** 0.5)
     return x, nw, wgu, wd
 
 
@@ -56,22 +59,48 @@ def _cpu_ops() -> SimpleNamespace:
     def silu_mul(g, u):
         return torch.from_numpy(ops.silu_mul(g.contiguous().numpy(), u.contiguous().numpy(), "bfloat16"))
 
-    return SimpleNamespace(rms_norm=rms_norm, gemm=gemm, silu_mul=silu_mul)
+    def rms_rstd(x, eps):
+        return torch.from_numpy(ops.rms_rstd(x.float().numpy(), eps))
+
+    def gemm_silu_mul(a, w, row_scale=None):
+        # w is [K, 2I] with gate and up interleaved in 128-column blocks
+        K, n2 = w.shape
+        blocks = w.float().reshape(K, n2 // 256, 2, 128)
+        wg = blocks[:, :, 0, :].reshape(K, n2 // 2).numpy()
+        wu = blocks[:, :, 1, :].reshape(K, n2 // 2).numpy()
+        a32 = a.float().numpy()
+        g, u = a32 @ wg, a32 @ wu
+        if row_scale is not None:
+            rs = row_scale.float().numpy().reshape(-1, 1)
+            g, u = g * rs, u * rs
+        return torch.from_numpy(ops.silu_mul(g, u, "bfloat16"))
+
+    return SimpleNamespace(rms_norm=rms_norm, gemm=gemm, silu_mul=silu_mul, rms_rstd=rms_rstd,
+                           gemm_silu_mul=gemm_silu_mul)
 
 
-def _rank_main(rank: int, world: int, port: int, chunks: int, out_dir: str, fail_rank: int) -> None:
+def _rank_main(rank: int, world: int, port: int, chunks: int, out_dir: str, fail_rank: int,
+               mode: str = "plain") -> None:
     for p in (REPO, REPO / "inference-kernel_b200"):
         sys.path.insert(0, str(p))
     import torch
     import torch.distributed as dist
 
-    from aot_kernel.tp_mlp import MLPShard, TensorParallelMLP, shard_down, shard_gate_up
+    from aot_kernel.tp_mlp import (MLPShard, TensorParallelMLP, shard_down, shard_gate_up,
+                                   shard_gate_up_folded, shard_gate_up_interleaved)
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=8))
-    x, nw, wgu, wd = (torch.from_numpy(a) for a in _weights())
-    shard = MLPShard(nw, shard_gate_up(wgu, rank, world), shard_down(wd, rank, world))
+    x, nw, wgu, wd = (torch.from_numpy(a) for a in _weights(mode))
+    if mode == "fold":
+        wgu_r = shard_gate_up_folded(wgu, nw, rank, world)
+    elif mode == "fused_silu":
+        wgu_r = shard_gate_up_interleaved(wgu, rank, world)
+    else:
+        wgu_r = shard_gate_up(wgu, rank, world)
+    shard = MLPShard(nw, wgu_r, shard_down(wd, rank, world), fused_silu=mode != "plain",
+                     fold_norm=mode == "fold")
     block = TensorParallelMLP(shard, chunks=chunks, ops=_cpu_ops())
     if rank == fail_rank:
         os._exit(3)  # a rank that dies before the collective
@@ -87,10 +116,12 @@ def _rank_main(rank: int, world: int, port: int, chunks: int, out_dir: str, fail
         pass
 
 
-def _launch(world: int, chunks: int, tmp_path, fail_rank: int = -1, timeout: float = 120.0):
+def _launch(world: int, chunks: int, tmp_path, fail_rank: int = -1, timeout: float = 120.0,
+            mode: str = "plain"):
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, chunks, str(tmp_path), fail_rank))
+    procs = [ctx.Process(target=_rank_main,
+                         args=(r, world, port, chunks, str(tmp_path), fail_rank, mode))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -117,6 +148,24 @@ def test_tp_block_matches_oracle(world, chunks, tmp_path):
         # every rank holds the same reduced output
         np.testing.assert_allclose(y, sharded, rtol=1e-2, atol=1e-2 * np.abs(sharded).max())
         assert np.abs(y - full).max() <= 2e-2 * np.abs(full).max()
+
+
+@pytest.mark.parametrize("world", [1, 2, 4])
+@pytest.mark.parametrize("mode", ["fused_silu", "fold"])
+def test_tp_block_fused_layouts_match_oracle(world, mode, tmp_path):
+    """The interleaved gate/up shard (fused silu) and the shard with the
+    rms_norm weight folded into its rows: each rank's block, reduced over the
+    group, matches the unsharded oracle block within the GEMM tolerance."""
+    from oracle import ops
+
+    procs = _launch(world, 1, tmp_path, mode=mode)
+    assert all(p.exitcode == 0 for p in procs)
+    x, nw, wgu, wd = _weights(mode)
+    full = ops.mlp_block(x, nw, wgu, wd, 1e-6, "bfloat16")
+    ys = [ops.round_to(np.load(tmp_path / f"y{r}.npy"), "bfloat16") for r in range(world)]
+    for r in range(1, world):
+        np.testing.assert_array_equal(ys[r], ys[0])
+    assert np.abs(ys[0] - full).max() <= 2e-2 * np.abs(full).max()
 
 
 def test_rank_failure_is_reported_not_hung(tmp_path):
