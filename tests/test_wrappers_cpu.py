@@ -52,3 +52,41 @@ def test_scaled_gemm_checks_before_device_work():
     with pytest.raises(RuntimeError):
         scaled_gemm(a, b, s, s)
     assert "scaled_gemm" in aot_kernel.__all__
+
+
+def test_interleave_and_fold_weights_on_cpu():
+    """The weight-layout helpers are plain torch and run on any device: the
+    interleaved [K, 2I] layout puts gate block j at columns [256j, 256j+128)
+    and up block j right after it; folding scales row k by norm_weight[k]
+    in fp32 and rounds once."""
+    from aot_kernel.gemm import fold_norm_weight, interleave_gate_up
+
+    K, inter = 8, 256
+    g = torch.arange(K * inter, dtype=torch.float32).reshape(K, inter).to(torch.bfloat16)
+    u = -g
+    w = interleave_gate_up(g, u)
+    assert w.shape == (K, 2 * inter)
+    assert torch.equal(w[:, 0:128], g[:, 0:128]) and torch.equal(w[:, 128:256], u[:, 0:128])
+    assert torch.equal(w[:, 256:384], g[:, 128:256]) and torch.equal(w[:, 384:512], u[:, 128:256])
+    nw = torch.linspace(0.5, 1.5, K).to(torch.bfloat16)
+    f = fold_norm_weight(w, nw)
+    assert f.dtype == w.dtype and f.shape == w.shape
+    assert torch.equal(f, (w.float() * nw.float().reshape(-1, 1)).to(torch.bfloat16))
+    with pytest.raises(ValueError):
+        interleave_gate_up(g[:, :100], u[:, :100])  # not a multiple of 128 columns
+    with pytest.raises(ValueError):
+        fold_norm_weight(w, nw[:-1])
+
+
+def test_gemm_host_checks_before_device_work():
+    from aot_kernel.gemm import gemm_host
+
+    a = torch.zeros(4, 8, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        gemm_host(a, torch.zeros(8, 4, dtype=torch.float32))  # dtype mismatch
+    with pytest.raises(ValueError):
+        gemm_host(a.float(), torch.zeros(8, 4))  # fp32: tensor-core dtypes only
+    with pytest.raises(ValueError):
+        gemm_host(a, torch.zeros(7, 4, dtype=torch.bfloat16))  # inner dims
+    with pytest.raises(ValueError):
+        gemm_host(a.t(), torch.zeros(4, 4, dtype=torch.bfloat16))  # not contiguous
