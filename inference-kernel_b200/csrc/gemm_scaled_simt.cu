@@ -129,8 +129,10 @@ int gemm_scaled_simt(void* c, const void* a, const void* b, const float* scale_a
   const int step = scale_mode == AOTK_SCALE_ROW ? 1 : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int m = (int)M, n = (int)N, k = (int)K;
-  if (in_dtype == AOTK_FLOAT8_E4M3) return launch<1>(c, a, b, scale_a, scale_b, step, m, n, k, out_dtype, s);
-  if (in_dtype == AOTK_FLOAT8_E5M2) return launch<2>(c, a, b, scale_a, scale_b, step, m, n, k, out_dtype, s);
+  if (in_dtype == AOTK_FLOAT8_E4M3)
+    return launch<1>(c, a, b, scale_a, scale_b, step, m, n, k, out_dtype, s);
+  if (in_dtype == AOTK_FLOAT8_E5M2)
+    return launch<2>(c, a, b, scale_a, scale_b, step, m, n, k, out_dtype, s);
   return launch<0>(c, a, b, scale_a, scale_b, step, m, n, k, out_dtype, s);
 }
 

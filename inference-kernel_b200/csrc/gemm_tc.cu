@@ -256,8 +256,9 @@ __device__ __forceinline__ void st_global_v4(float* p, uint32_t a, uint32_t b, u
 // Fused all-reduce of the output over W ranks (one process per GPU) through
 // NVSwitch multicast memory.  Each rank stores its partial tile into its own
 // `part` buffer, then bumps the tile's arrival counter on the owner rank
-// (tile_owner: rotates over the ranks from round to round).  The owner's all-reduce warps wait until all W partials of the
-// tile have arrived, read their sum through the multicast address of `part`
+// (tile_owner: rotates over the ranks from round to round).  The owner's
+// all-reduce warps wait until all W partials of the tile have arrived, read
+// their sum through the multicast address of `part`
 // (multimem.ld_reduce, fp32 accumulation) and write it to every rank's `out`
 // through the multicast address of `out` (multimem.st).  Counters only grow:
 // call number e (epoch, from 1) waits for W*e arrivals.  A final done
@@ -1132,7 +1133,8 @@ int gemm_allreduce(const void* a, const void* b, int64_t M, int64_t N, int64_t K
                 "aotk_gemm_allreduce: incomplete buffers (rank %d of %d, epoch %u)", bufs->rank,
                 bufs->world, bufs->epoch);
   if ((bufs->part_multicast & 15u) || (bufs->out_multicast & 15u))
-    return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_gemm_allreduce: multicast addresses not 16-byte aligned");
+    return fail(AOTK_ERR_INVALID_ARGUMENT,
+                "aotk_gemm_allreduce: multicast addresses not 16-byte aligned");
   ArParams ar{};
   ar.rank = bufs->rank;
   ar.world = bufs->world;

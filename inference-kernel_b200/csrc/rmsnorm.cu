@@ -303,12 +303,17 @@ int launch_rstd(const void* xv, float* rstd, int64_t rows, int64_t cols, float e
   // mode (the same row layout and prefetch as rms_norm, no output row).
   if (cols % E == 0 && aligned16(x) && n_vec <= 8 * 1024 && n_vec > 128) {
     const int nv = (int)n_vec, c = (int)cols;
-    if (nv <= 8 * 32) return launch_vec<T, 8, 32, false, true>(x, nullptr, nullptr, nullptr, nullptr, rows, c, eps, s, rstd);
-    if (nv <= 8 * 64) return launch_vec<T, 8, 64, false, true>(x, nullptr, nullptr, nullptr, nullptr, rows, c, eps, s, rstd);
-    if (nv <= 8 * 128) return launch_vec<T, 8, 128, false, true>(x, nullptr, nullptr, nullptr, nullptr, rows, c, eps, s, rstd);
-    if (nv <= 8 * 256) return launch_vec<T, 8, 256, false, true>(x, nullptr, nullptr, nullptr, nullptr, rows, c, eps, s, rstd);
-    if (nv <= 8 * 512) return launch_vec<T, 8, 512, false, true>(x, nullptr, nullptr, nullptr, nullptr, rows, c, eps, s, rstd);
-    return launch_vec<T, 8, 1024, false, true>(x, nullptr, nullptr, nullptr, nullptr, rows, c, eps, s, rstd);
+    const T* none = nullptr;
+    T* none_out = nullptr;
+#define AOTK_RSTD_VEC(TPR) \
+  launch_vec<T, 8, TPR, false, true>(x, none, none, none_out, none_out, rows, c, eps, s, rstd)
+    if (nv <= 8 * 32) return AOTK_RSTD_VEC(32);
+    if (nv <= 8 * 64) return AOTK_RSTD_VEC(64);
+    if (nv <= 8 * 128) return AOTK_RSTD_VEC(128);
+    if (nv <= 8 * 256) return AOTK_RSTD_VEC(256);
+    if (nv <= 8 * 512) return AOTK_RSTD_VEC(512);
+    return AOTK_RSTD_VEC(1024);
+#undef AOTK_RSTD_VEC
   }
   const int64_t blocks = (rows + kBlock / 32 - 1) / (kBlock / 32);
   if (blocks > 0x7fffffffLL) return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_rmsnorm_rstd: too many rows");
