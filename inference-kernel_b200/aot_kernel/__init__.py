@@ -6,8 +6,11 @@ by ``inference-kernel_b200/build.py``), which registers ``torch.ops.aot_kernel.*
 and pulls in ``libaotk.so`` (the CUDA kernels and their C ABI).  Names and
 signatures follow the reference's ``aot_kernel/__init__.py:8-20``; ``rms_norm``
 is an alias of ``rmsnorm``; ``silu_mul``, ``add_rmsnorm`` and ``gemm_silu_mul``
-are new fused ops; ``scaled_gemm`` is the reference's 8-bit GEMM
-(``jit_kernel.gemm.scaled_gemm``, a Triton kernel there) with the same signature.
+are new fused ops (``interleave_gate_up`` builds the fused gate/up weight,
+``fold_norm_weight`` and ``rms_rstd`` fold rms_norm into it); ``scaled_gemm`` is
+the reference's 8-bit GEMM (``jit_kernel.gemm.scaled_gemm``, a Triton kernel
+there) with the same signature; ``gemm_host`` runs ``gemm`` on host-resident
+operands with the copies overlapped.
 """
 
 from .activation import relu, silu, silu_mul
