@@ -57,6 +57,7 @@ CASES = {
     "gemm_decode_m1": ("gemm", (1, 4096, 28672)),
     "gemm_decode_m16": ("gemm", (16, 4096, 28672)),
     "gemm_m128_down": ("gemm", (128, 14336, 4096)),
+    "gate_up_silu_2048": ("gate_up_silu", (2048, 4096, 14336)),
     "scaled_gemm_fp8_8192": ("scaled_gemm_e4m3", (8192, 8192, 8192)),
     "scaled_gemm_fp8_4096": ("scaled_gemm_e4m3", (4096, 4096, 4096)),
     "scaled_gemm_int8_4096": ("scaled_gemm_int8", (4096, 4096, 4096)),
@@ -695,6 +696,11 @@ def run_case(args) -> None:
         a = rand_bf16((M, K), 1)
         b = rand_bf16((K, N), 2, std=0.02)
         fn = lambda: aot_kernel.gemm(a, b)  # noqa: E731
+    elif kind == "gate_up_silu":
+        M, K, inter = shape
+        a = rand_bf16((M, K), 1)
+        w = rand_bf16((K, 2 * inter), 2, std=0.02)
+        fn = lambda: aot_kernel.gemm_silu_mul(a, w)  # noqa: E731
     elif kind.startswith("scaled_gemm"):
         M, K, N = shape
         q = kind.rsplit("_", 1)[1]
