@@ -603,7 +603,6 @@ def cpu_baseline(target_s: float = 8.0) -> dict:
     as one line, is the timed value.  The numpy oracle (float32 BLAS) is timed
     beside it for reference.
     """
-    import numpy as np
     import torch
 
     from oracle import ops

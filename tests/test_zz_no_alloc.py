@@ -7,10 +7,9 @@ file, named to be collected last."""
 
 from __future__ import annotations
 
-import numpy as np
 import pytest
 
-from tests.conftest import assert_close_for_gemm, to_device
+from tests.conftest import to_device
 from oracle.inputs import randn
 
 pytestmark = pytest.mark.gpu
