@@ -169,3 +169,24 @@ def test_sharded_block_matches_unsharded_block():
         part = ops.mlp_block_sharded(x, nw, wgu, wd, 1e-6, "bfloat16", world)
         err = np.max(np.abs(part - full))
         assert err <= 2e-2 * np.max(np.abs(full))
+
+
+def test_folded_norm_oracle_tracks_the_reference_composition():
+    """gemm_silu_mul_folded (rms_norm folded into the weight rows and the
+    accumulator) against the reference composition ref.rmsnorm -> ref.gemm
+    -> ref.silu(gate) * up restated by the pinned primitives: within the
+    GEMM tolerance, and rms_rstd is the factor rmsnorm applies."""
+    from oracle.inputs import randn
+
+    x = randn((64, 512), 11)
+    nw = randn((512,), 12, mean=1.0, std=0.1)
+    wg = randn((512, 256), 13, std=512 ** -0.5)
+    wu = randn((512, 256), 14, std=512 ** -0.5)
+    folded = ops.gemm_silu_mul_folded(x, nw, wg, wu, 1e-6, "bfloat16")
+    h = ops.rmsnorm(x, nw, 1e-6, "bfloat16")
+    composed = ops.silu_mul_composed(ops.gemm(h, wg, "bfloat16"), ops.gemm(h, wu, "bfloat16"),
+                                     "bfloat16")
+    assert np.abs(folded - composed).max() <= 2e-2 * np.abs(composed).max()
+    rstd = ops.rms_rstd(x, 1e-6)
+    unit = ops.rmsnorm(x, np.ones(512, np.float32), 1e-6, "float32")
+    np.testing.assert_allclose(unit, x * rstd.reshape(-1, 1), rtol=1e-6, atol=0)
