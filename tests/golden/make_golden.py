@@ -17,6 +17,7 @@ from __future__ import annotations
 import argparse
 import hashlib
 import json
+import os
 import sys
 from pathlib import Path
 
@@ -90,7 +91,9 @@ def input_digest(x: np.ndarray, case) -> str:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference", help="reference checkout (read-only)")
+    ap.add_argument("--reference", default=os.environ.get("AOTK_REFERENCE_DIR"),
+                    required="AOTK_REFERENCE_DIR" not in os.environ,
+                    help="reference checkout, read only (default: $AOTK_REFERENCE_DIR)")
     args = ap.parse_args()
     sys.path.insert(0, str(REPO))
     sys.path.insert(0, str(HERE))
