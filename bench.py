@@ -1,29 +1,34 @@
 #!/usr/bin/env python
 """Benchmark of the dense-linear inference path on B200.
 
-Headline (one JSON line on rank 0): bf16 GEMM TFLOP/s on the square
-M = N = K = 8192 problem (fp32 accumulation, bf16 output) through the
-``aot_kernel`` public API.  A step is one GEMM over operands already resident
-in HBM; at N GPUs every rank runs its own GEMM (independent replicas, weak
-scaling) and ``value`` is the sum over ranks.  The same line carries:
+Headline (one JSON line on rank 0): tokens/s of the Llama-3-70B MLP block -
+x[4096 tokens, 8192] -> rms_norm -> gate/up GEMM 8192 -> 2 x 28672 ->
+silu(gate) * up -> down GEMM 28672 -> 8192 -> all-reduce - tensor-parallel
+over the N ranks of one node (N = 1, 2, 4, 8; strong scaling: the same 4096
+tokens per step at every N).  A step is one pass of the block over inputs
+already resident in HBM; ``value`` is 4096 * steps / (max over ranks of the
+CUDA-event time of the timed steps).  Per rank the block is three kernels:
+rms_rstd (rms_norm's row statistic), the gate/up GEMM with rms_norm folded in
+and silu(gate) * up in its epilogue, and the down GEMM fused with an NVSwitch
+all-reduce (N > 1) or the plain down GEMM (N = 1).  The line also carries:
 
-* ``roofline``  - the GEMM kernel's achieved TFLOP/s (2*M*N*K / mean CUDA-event
-  duration of its launches) against the measured bf16 peak;
-* ``e2e``       - the same metric through the public API with pinned host
-  buffers: host->device copy of A and B, the GEMM, device->host copy of C;
-* ``cpu_baseline`` - the reference's CPU GEMM (``a @ b`` on CPU bf16 tensors,
-  all host threads) on a bounded row sample of the same problem, with the
-  numpy oracle's rate beside it (rank 0, N = 1);
-* ``kernels``   - the remaining workloads of the path at their configured sizes:
-  the square sweep, the Llama-3-8B linear layers from decode to prefill,
-  rms_norm, silu and silu(gate)*up, each with its roofline fraction (N = 1);
-* ``tp_mlp``    - tokens/s of the Llama-3-70B MLP block (4096 tokens,
-  hidden 8192, intermediate 28672) tensor-parallel over the N ranks with one
-  NCCL all-reduce (the multi-GPU path; strong scaling in tokens).
+* ``roofline``  - the gate/up GEMM (the dominant kernel, 2/3 of the flops):
+  2 * T * H * 2I / N flops per launch / its mean CUDA-event duration in the
+  timed steps, against the measured bf16 peak;
+* ``e2e``       - the same tokens/s through ``aot_kernel.tp_mlp.HostStream``
+  with pinned HOST batches: every step copies its input rows in, runs the
+  block, and copies its output rows back, inside the timed region;
+* ``tp_parity`` - sampled rows of the block's output against the reference
+  composition (ref.rmsnorm -> ref.gemm -> ref.silu(gate) * up -> ref.gemm)
+  run on CPU by torch, max|err| <= 2e-2 * max|ref|;
+* ``cpu_baseline`` - that reference composition timed on the host's cores on
+  the full 4096-token block (rank 0, N = 1);
+* ``kernels`` (N = 1) - every other configured workload with its roofline
+  fraction: the square GEMM sweep, the Llama-3-8B linears from decode to
+  prefill, rms_norm, silu, silu(gate) * up, 8-bit GEMMs, and ``gemm_8192``.
 
-``--impl reference`` times the reference's CPU path (``ref.gemm`` = ``a @ b``
-on CPU tensors, all host threads) on the same metric instead; under torchrun
-only rank 0 runs it.
+``--impl reference`` times that reference composition on the host's cores on
+the same block and metric instead; under torchrun only rank 0 runs it.
 
 ``--case NAME`` runs only NAME's launches (warmup + steps) and prints nothing
 else: the command the committed ncu summaries under profiles/ were made with.
@@ -32,11 +37,13 @@ else: the command the committed ncu summaries under profiles/ were made with.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 import statistics
 import sys
 import time
+import traceback
 from datetime import timedelta
 from pathlib import Path
 
@@ -46,22 +53,33 @@ for _p in (REPO, REPO / "inference-kernel_b200"):
         sys.path.insert(0, str(_p))
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-HEADLINE = (8192, 8192, 8192)
 L2_BYTES = 126 * 1024 * 1024
-
+TOKENS, HIDDEN, INTER = 4096, 8192, 28672
+EPS = 1e-6
+BLOCK_FLOPS = 2.0 * TOKENS * HIDDEN * 2 * INTER + 2.0 * TOKENS * INTER * HIDDEN
+PARITY_ROWS = 32
+PARITY_TOL = 2e-2
 
 # --case workloads: name -> (kind, shape)
 CASES = {
     "gemm_8192": ("gemm", (8192, 8192, 8192)),
     "gemm_4096": ("gemm", (4096, 4096, 4096)),
+    "gemm_tc2_8192": ("gemm_tc2", (8192, 8192, 8192)),
     "gemm_decode_m1": ("gemm", (1, 4096, 28672)),
     "gemm_decode_m16": ("gemm", (16, 4096, 28672)),
+    "gemm_qkv_m1": ("gemm", (1, 4096, 6144)),
+    "gemm_qkv_m128": ("gemm", (128, 4096, 6144)),
     "gemm_m128_down": ("gemm", (128, 14336, 4096)),
     "gate_up_silu_2048": ("gate_up_silu", (2048, 4096, 14336)),
+    "tp_gate_up_tp1": ("tp_gate_up", (TOKENS, HIDDEN, INTER)),
+    "tp_gate_up_tp8": ("tp_gate_up", (TOKENS, HIDDEN, INTER // 8)),
+    "tp_down_tp1": ("gemm", (TOKENS, INTER, HIDDEN)),
     "scaled_gemm_fp8_8192": ("scaled_gemm_e4m3", (8192, 8192, 8192)),
     "scaled_gemm_fp8_4096": ("scaled_gemm_e4m3", (4096, 4096, 4096)),
     "scaled_gemm_int8_4096": ("scaled_gemm_int8", (4096, 4096, 4096)),
     "rms_norm": ("rms_norm", (8192, 4096)),
+    "rms_rstd": ("rms_rstd", (8192, 4096)),
+    "rms_rstd_tp": ("rms_rstd", (TOKENS, HIDDEN)),
     "add_rms_norm": ("add_rms_norm", (8192, 4096)),
     "silu": ("silu", (8192, 14336)),
     "silu_mul": ("silu_mul", (8192, 14336)),
@@ -75,7 +93,6 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-kernels", action="store_true", help="skip the per-workload table")
-    ap.add_argument("--no-tp", action="store_true", help="skip the tensor-parallel MLP block")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--tp-chunks", type=int, default=1)
     ap.add_argument("--tp-allreduce", choices=["nccl", "fused"], default="fused",
@@ -221,94 +238,236 @@ def row_scales(M: int, N: int, seed: int):
     return sa, sb
 
 
-def headline_gemm(args, rank: int, world: int, peaks: dict):
+# ---------------------------------------------------------------- the block on the GPU
+
+def tp_build(args, rank: int, world: int):
+    """The block's inputs drawn on the device (seeded Philox), sharded for this
+    rank.  Rank 0 keeps host copies of x, the norm weight and the full
+    weights for the parity check and the CPU baseline."""
+    import torch
+
+    from aot_kernel.tp_mlp import (MLPShard, TensorParallelMLP, shard_down, shard_gate_up,
+                                   shard_gate_up_folded, shard_gate_up_interleaved)
+
+    x = rand_bf16((TOKENS, HIDDEN), 30)
+    nw = rand_bf16((HIDDEN,), 31, std=0.1, mean=1.0)
+    w_gu = rand_bf16((HIDDEN, 2 * INTER), 32, std=0.02)
+    host = {}
+    if rank == 0:
+        host.update(x=x.cpu(), nw=nw.cpu(), wgu=w_gu.cpu())
+    fused_silu = not args.tp_unfused_silu
+    fold_norm = fused_silu and not args.tp_unfolded_norm
+    if fold_norm:
+        wgu_r = shard_gate_up_folded(w_gu, nw, rank, world)
+    else:
+        wgu_r = (shard_gate_up_interleaved if fused_silu else shard_gate_up)(w_gu, rank, world)
+    del w_gu
+    w_d = rand_bf16((INTER, HIDDEN), 33, std=0.02)
+    if rank == 0:
+        host["wd"] = w_d.cpu()
+    wd_r = shard_down(w_d, rank, world)
+    del w_d
+    torch.cuda.empty_cache()
+    allreduce = args.tp_allreduce if world > 1 else "nccl"
+    block = TensorParallelMLP(MLPShard(nw, wgu_r, wd_r, fused_silu=fused_silu, fold_norm=fold_norm),
+                              eps=EPS, chunks=args.tp_chunks, allreduce=allreduce)
+    return x, block, host
+
+
+def _max_over_ranks(vals: list[float], world: int) -> list[float]:
     import torch
     import torch.distributed as dist
 
-    import aot_kernel
+    t = torch.tensor(vals, device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
 
-    M, N, K = HEADLINE
-    a = rand_bf16((M, K), 1 + rank)
-    b = rand_bf16((K, N), 2 + rank, std=K ** -0.5)
-    flops = 2.0 * M * N * K
 
-    def step():
-        return aot_kernel.gemm(a, b)
+def _meet(world: int) -> None:
+    import torch
+    import torch.distributed as dist
 
-    for _ in range(args.warmup):
-        step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+
+
+def tp_timed(args, block, x, world: int, peaks: dict, guard) -> dict:
+    """Exactly ``args.steps`` block steps between two events, after
+    ``args.warmup`` untimed ones.  Inside every timed step, events before the
+    block, around its gate/up GEMM launch and after it split the step into
+    rms_rstd | gate/up GEMM | down GEMM (+ all-reduce)."""
+    import torch
+
+    for _ in range(args.warmup):
+        block(x)
+    _meet(world)
+    guard.check()
+
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+
     with ClockSampler(torch.cuda.current_device()) as clocks:
-        events = []
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
+        evs = [(ev(), ev(), ev(), ev()) for _ in range(args.steps)]
+        t0, t1 = ev(), ev()
         t0.record()
-        for _ in range(args.steps):
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record()
-            step()
-            e.record()
-            events.append((s, e))
+        for a, b, c, d in evs:
+            a.record()
+            block(x, gate_up_events=(b, c))
+            d.record()
         t1.record()
         torch.cuda.synchronize()
     total_ms = t0.elapsed_time(t1)
-    launch_ms = statistics.mean(s.elapsed_time(e) for s, e in events)
-    if world > 1:
-        dist.barrier()
-    t = torch.tensor([total_ms, launch_ms], device="cuda", dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms, launch_ms = t.tolist()
+    pre = statistics.mean(a.elapsed_time(b) for a, b, _, _ in evs)
+    gu_ms = statistics.mean(b.elapsed_time(c) for _, b, c, _ in evs)
+    post = statistics.mean(c.elapsed_time(d) for _, _, c, d in evs)
+    total_ms, pre, gu_ms, post = _max_over_ranks([total_ms, pre, gu_ms, post], world)
+    s = block.shard
+    first = "rms_rstd" if s.fold_norm else "rms_norm"
+    mid = "gate_up+norm+silu" if s.fold_norm else ("gate_up+silu" if s.fused_silu else "gate_up")
+    last = ("" if s.fused_silu else "silu_mul+") + ("down" if world == 1 else "down+all_reduce")
+    gu_flops = 2.0 * TOKENS * HIDDEN * 2 * INTER / world
+    achieved = gu_flops / (gu_ms * 1e-3) / 1e12
+    return {"ms_per_step": total_ms / args.steps,
+            "value": TOKENS * args.steps / (total_ms * 1e-3),
+            "phases_ms": {first: round(pre, 4), mid: round(gu_ms, 4), last: round(post, 4)},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1),
+                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": round(achieved / peaks["bf16_tflops"], 4),
+                         "traffic": traffic_per_launch(f"tp_gate_up_tp{world}"),
+                         "kernel": f"gemm_silu_mul + folded rms_norm, M={TOKENS} K={HIDDEN} "
+                                   f"N={2 * INTER // world}"},
+            "gpu_launches": block.launches_per_step() * args.steps,
+            "clocks": clocks.summary()}
 
-    # End to end through the public host-buffer API (aot_kernel.gemm_host ->
-    # aotk_gemm_host): every step copies A and B in from pinned host memory and
-    # C back out, overlapped with the GEMM row blocks.
-    a_h = a.cpu().pin_memory()
-    b_h = b.cpu().pin_memory()
-    c_h = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
 
-    def e2e_step():
-        aot_kernel.gemm_host(a_h, b_h, out=c_h)
+def tp_e2e(args, block, x, rank: int, world: int, guard) -> dict:
+    """The block through ``HostStream``: pinned host batch in, block, output
+    rows back to pinned host memory, every step, inside the timed region."""
+    import torch
 
-    e2e_steps = max(3, min(args.steps, 20))
+    from aot_kernel.tp_mlp import HostStream
+
+    hs = HostStream(block, TOKENS, HIDDEN, x.device)
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty((TOKENS, HIDDEN), dtype=torch.bfloat16).pin_memory()
     for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+        hs.submit(x_host, out_host)
+    hs.drain()
+    _meet(world)
+    guard.check()
+    cur = torch.cuda.current_stream()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
-    for _ in range(e2e_steps):
-        e2e_step()
+    hs.h2d.wait_stream(cur)  # the first copy-in starts after the start event
+    for _ in range(args.steps):
+        hs.submit(x_host, out_host)
+    hs.drain()
     e.record()
     torch.cuda.synchronize()
-    e2e_ms = torch.tensor([s.elapsed_time(e) / e2e_steps], device="cuda", dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_ms = float(e2e_ms.item())
+    (ms,) = _max_over_ranks([s.elapsed_time(e) / args.steps], world)
+    # the rows this rank read back equal the device-resident block's output
+    y = block(x)
+    diff = (out_host[hs.lo:hs.hi].float() - y[hs.lo:hs.hi].float().cpu()).abs().max().item()
+    (diff,) = _max_over_ranks([diff], world)
+    return {"value": TOKENS / (ms * 1e-3), "unit": "tokens/s",
+            "h2d_bytes_per_step": hs.h2d_bytes() * world, "d2h_bytes_per_step": hs.d2h_bytes() * world,
+            "ms_per_step": round(ms, 4), "max_abs_diff_vs_device": diff,
+            "api": "aot_kernel.tp_mlp.HostStream.submit(x_host, out_host): each rank copies its "
+                   "1/N of the pinned input rows in, all-gather over NVLink, block, its 1/N of the "
+                   "output rows back; next batch's copy-in overlaps this batch's kernels"}
 
-    achieved = flops / (launch_ms * 1e-3) / 1e12
-    res = {
-        "value": world * flops * args.steps / (total_ms * 1e-3) / 1e12,
-        "ms_per_step": total_ms / args.steps,
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
-                     "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
-                     "traffic": traffic_per_launch("gemm_tc_8192")},
-        "e2e": {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                "h2d_bytes_per_step": a.nbytes + b.nbytes, "d2h_bytes_per_step": M * N * 2,
-                "ms_per_step": e2e_ms,
-                "api": "aot_kernel.gemm_host (C ABI aotk_gemm_host): pinned host A, B, C; "
-                       "B then 128-row-multiple blocks of A copied in, C blocks copied out, "
-                       "overlapped with the GEMM blocks"},
-        "gpu_launches": args.steps,
-        "clocks": clocks.summary(),
-    }
-    del a_h, b_h, c_h
-    return res
 
+def tp_parity(block, x, host: dict, rank: int) -> dict | None:
+    """Sampled output rows against the reference composition on CPU."""
+    import torch
+
+    y = block(x)  # every rank takes part (the all-reduce)
+    torch.cuda.synchronize()
+    if rank != 0:
+        return None
+    rows = torch.randperm(TOKENS, generator=torch.Generator().manual_seed(5))[:PARITY_ROWS].sort().values
+    got = y[rows.cuda()].float().cpu()
+    ref = reference_block_cpu(host["x"][rows], host["nw"], host["wgu"], host["wd"]).float()
+    err = (got - ref).abs().max().item()
+    scale = ref.abs().max().item()
+    return {"rows": PARITY_ROWS, "max_abs_err": err, "max_abs_ref": scale,
+            "err_frac": round(err / scale, 6), "tol_frac": PARITY_TOL,
+            "pass": bool(err <= PARITY_TOL * scale),
+            "reference": "ref.rmsnorm -> ref.gemm -> ref.silu(gate) * up -> ref.gemm (torch CPU)"}
+
+
+# ---------------------------------------------------------------- the reference on the host
+
+def reference_block_cpu(x, nw, wgu, wd, eps: float = EPS):
+    """The reference's MLP block on CPU tensors, one torch call per reference
+    op: ref.rmsnorm = F.rms_norm(x, (H,), w, eps) (ref/norm.py:11-12),
+    ref.gemm = a @ b (ref/gemm.py:4-5), ref.silu = F.silu
+    (ref/activation.py:15-16); silu(gate) * up as ref.silu(gate) * up."""
+    import torch.nn.functional as F
+
+    h = F.rms_norm(x, (x.shape[-1],), nw, eps)
+    gu = h @ wgu
+    inter = wgu.shape[1] // 2
+    act = F.silu(gu[:, :inter]) * gu[:, inter:]
+    return act @ wd
+
+
+def _cpu_inputs(seed: int = 0):
+    """Block inputs for a CPU-only run, bf16: x ~ N(0, 1), norm weight
+    N(1, 0.1), weights N(0, 0.02).  The weights are tiled from a seeded pool
+    of 2^24 samples (drawing 700 M samples one by one would take longer than
+    the timing itself; the GEMM's speed does not depend on the values)."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    pool = torch.randn(1 << 24, generator=g)
+
+    def tiled(shape, std, offset):
+        n = shape[0] * shape[1]
+        reps = -(-(n + offset) // pool.numel())
+        flat = pool.repeat(reps)[offset:offset + n]
+        return (flat * std).to(torch.bfloat16).reshape(shape)
+
+    x = torch.randn((TOKENS, HIDDEN), generator=g).to(torch.bfloat16)
+    nw = (torch.randn((HIDDEN,), generator=g) * 0.1 + 1.0).to(torch.bfloat16)
+    return x, nw, tiled((HIDDEN, 2 * INTER), 0.02, 12345), tiled((INTER, HIDDEN), 0.02, 777)
+
+
+def cpu_block_times(x, nw, wgu, wd, steps: int, warmup: int, budget_s: float | None = None):
+    """Seconds per reference block step on the host, all threads."""
+    import torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    for _ in range(warmup):
+        reference_block_cpu(x, nw, wgu, wd)
+    times = []
+    t_all = time.perf_counter()
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        reference_block_cpu(x, nw, wgu, wd)
+        times.append(time.perf_counter() - t0)
+        if budget_s is not None and time.perf_counter() - t_all >= budget_s:
+            break
+    return times, torch.get_num_threads()
+
+
+def cpu_baseline(host: dict) -> dict:
+    """The reference composition on the host's cores, on the same 4096-token
+    block and weights as the GPU run (a bounded number of steps)."""
+    times, cores = cpu_block_times(host["x"], host["nw"], host["wgu"], host["wd"], steps=8,
+                                   warmup=1, budget_s=15.0)
+    mean = statistics.mean(times)
+    return {"value": TOKENS / mean, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"the full block (4096 tokens, same inputs) x {len(times)} steps, "
+                      f"{mean * 1e3:.0f} ms per step; torch CPU composition of ref.rmsnorm, "
+                      f"ref.gemm, ref.silu",
+            "cpu_count": os.cpu_count()}
+
+
+# ---------------------------------------------------------------- per-workload table (N = 1)
 
 def traffic_per_launch(key: str):
     p = REPO / "profiles" / "traffic.json"
@@ -355,8 +514,36 @@ def _sets_for(nbytes: int, cap: int = 16) -> int:
     return max(1, min(cap, -(-2 * L2_BYTES // max(1, nbytes))))
 
 
+def gemm_8192(args, peaks: dict) -> dict:
+    """The square 8192^3 bf16 GEMM through aot_kernel.gemm: args.steps launches
+    after args.warmup, each bracketed by CUDA events (operands 256 MB > L2)."""
+    import torch
+
+    import aot_kernel
+
+    n = 8192
+    a = rand_bf16((n, n), 1)
+    b = rand_bf16((n, n), 2, std=n ** -0.5)
+    for _ in range(args.warmup):
+        aot_kernel.gemm(a, b)
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    for s, e in evs:
+        s.record()
+        aot_kernel.gemm(a, b)
+        e.record()
+    torch.cuda.synchronize()
+    ms = statistics.mean(s.elapsed_time(e) for s, e in evs)
+    tf = 2.0 * n ** 3 / (ms * 1e-3) / 1e12
+    return {"ms": round(ms, 4), "tflops": round(tf, 1), "frac": round(tf / peaks["bf16_tflops"], 4),
+            "traffic": traffic_per_launch("gemm_tc_8192")}
+
+
 def kernel_table(peaks: dict) -> dict:
-    """Every configured workload of the path, timed from CUDA-graph replays."""
+    """Every configured workload of the path, timed from CUDA-graph replays.
+    Entries are [ms, TFLOP/s or GB/s, fraction of the measured peak] (the
+    8-bit GEMMs: [ms, TFLOP/s, ratio to the library kernel])."""
     import torch
 
     import aot_kernel
@@ -375,18 +562,17 @@ def kernel_table(peaks: dict) -> dict:
         del sets, outs, calls
         flops = 2.0 * M * N * K
         nbytes = 2.0 * (M * K + K * N + M * N)
-        tf = flops / (ms * 1e-3) / 1e12
+        if flops / nbytes >= ridge:
+            tf = flops / (ms * 1e-3) / 1e12
+            return [round(ms, 5), round(tf, 1), round(tf / peaks["bf16_tflops"], 3)]
         gbs = nbytes / (ms * 1e-3) / 1e9
-        bound = "tensor" if flops / nbytes >= ridge else "hbm"
-        frac = tf / peaks["bf16_tflops"] if bound == "tensor" else gbs / peaks["hbm_gbs"]
-        return {"ms": round(ms, 5), "tflops": round(tf, 2), "gbs": round(gbs, 1), "bound": bound,
-                "frac": round(frac, 4), "input_sets": R}
+        return [round(ms, 5), round(gbs, 1), round(gbs / peaks["hbm_gbs"], 3)]
 
     for n in (2048, 4096, 8192, 16384):
         out[f"gemm_{n}^3"] = gemm_entry(n, n, n, 10 + n, n ** -0.5)
     for K, N in ((4096, 6144), (4096, 28672), (14336, 4096)):
         for M in (1, 16, 128, 2048, 8192):
-            out[f"linear_M{M}_K{K}_N{N}"] = gemm_entry(M, K, N, M + K + N, 0.02)
+            out[f"lin_M{M}_K{K}_N{N}"] = gemm_entry(M, K, N, M + K + N, 0.02)
     for M in (2048, 8192):  # Llama-3-8B gate/up (I = 14336) with the fused silu epilogue
         K, inter = 4096, 14336
         a = rand_bf16((M, K), 50 + M)
@@ -394,9 +580,8 @@ def kernel_table(peaks: dict) -> dict:
         o = torch.empty((M, inter), device="cuda", dtype=torch.bfloat16)
         ms = graph_launch_ms([lambda: torch.ops.aot_kernel.gemm_silu_mul(o, a, w)])
         tf = 2.0 * M * K * 2 * inter / (ms * 1e-3) / 1e12
-        out[f"gate_up_silu_M{M}_K{K}_I{inter}"] = {"ms": round(ms, 5), "tflops": round(tf, 2),
-                                                   "bound": "tensor",
-                                                   "frac": round(tf / peaks["bf16_tflops"], 4)}
+        out[f"gate_up_silu_M{M}_K{K}_I{inter}"] = [round(ms, 5), round(tf, 1),
+                                                   round(tf / peaks["bf16_tflops"], 3)]
         del a, w, o
     torch.cuda.empty_cache()
 
@@ -416,271 +601,104 @@ def kernel_table(peaks: dict) -> dict:
                  for (a, b), c in zip(sets, outs)]
         ms = graph_launch_ms(calls)
         tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
-        entry = {"ms": round(ms, 5), "tflops": round(tf, 2), "bound": "tensor", "input_sets": R}
+        entry = [round(ms, 5), round(tf, 1), None]
         cols = [b.t().contiguous().t() for _, b in sets]  # [K, N] views of [N, K] storage
         del outs, calls
         try:
             if qdtype == "int8":
                 lib = [lambda a=a, bc=bc: (torch._int_mm(a, bc).float() * sa[:, None] * sb[None, :])
                        .to(torch.bfloat16) for (a, _), bc in zip(sets, cols)]
-                name = "torch._int_mm + dequant"
             else:
                 sa2, sb2 = sa.reshape(M, 1), sb.reshape(1, N)
                 lib = [lambda a=a, bc=bc: torch._scaled_mm(a, bc, scale_a=sa2, scale_b=sb2,
                                                            out_dtype=torch.bfloat16)
                        for (a, _), bc in zip(sets, cols)]
-                name = "torch._scaled_mm (cuBLASLt)"
-            lms = graph_launch_ms(lib)
-            ltf = 2.0 * M * N * K / (lms * 1e-3) / 1e12
-            entry["library"] = {"name": name, "ms": round(lms, 5), "tflops": round(ltf, 2)}
-            entry["frac_of_library"] = round(tf / ltf, 4)
-        except Exception as e:  # noqa: BLE001  (library path unavailable on this build)
-            entry["library"] = {"unavailable": str(e).splitlines()[0][:160]}
+            entry[2] = round(graph_launch_ms(lib) / ms, 3)
+        except Exception:  # noqa: BLE001  (library path unavailable on this build)
+            pass
         del sets, cols
         torch.cuda.empty_cache()
         return entry
 
     for n in (4096, 8192):
-        out[f"scaled_gemm_fp8_{n}^3"] = scaled_entry(n, "e4m3", 70 + n)
-        out[f"scaled_gemm_int8_{n}^3"] = scaled_entry(n, "int8", 80 + n)
+        out[f"fp8_{n}^3_vs_cublaslt"] = scaled_entry(n, "e4m3", 70 + n)
+        out[f"int8_{n}^3_vs_torch"] = scaled_entry(n, "int8", 80 + n)
 
-    def hbm_entry(calls, nbytes, R):
+    def hbm_entry(calls, nbytes):
         ms = graph_launch_ms(calls)
         gbs = nbytes / (ms * 1e-3) / 1e9
-        return {"ms": round(ms, 5), "gbs": round(gbs, 1), "bound": "hbm",
-                "frac": round(gbs / peaks["hbm_gbs"], 4), "bytes": int(nbytes), "input_sets": R}
+        return [round(ms, 5), round(gbs, 1), round(gbs / peaks["hbm_gbs"], 3)]
 
     rows, cols = 8192, 4096
     R = _sets_for(rows * cols * 2)
     w = rand_bf16((cols,), 21, std=0.1, mean=1.0)
     xs = [rand_bf16((rows, cols), 20 + 2 * i) for i in range(R)]
     out["rms_norm_8192x4096"] = hbm_entry([lambda x=x: aot_kernel.rms_norm(x, w) for x in xs],
-                                          2.0 * rows * cols * 2 + cols * 2, R)
+                                          2.0 * rows * cols * 2 + cols * 2)
     out["rms_rstd_8192x4096"] = hbm_entry([lambda x=x: aot_kernel.rms_rstd(x) for x in xs],
-                                          1.0 * rows * cols * 2 + rows * 4, R)
+                                          1.0 * rows * cols * 2 + rows * 4)
     rs = [rand_bf16((rows, cols), 40 + 2 * i) for i in range(R)]
     out["add_rms_norm_8192x4096"] = hbm_entry(
         [lambda x=x, r=r: aot_kernel.add_rmsnorm(x, r, w) for x, r in zip(xs, rs)],
-        4.0 * rows * cols * 2 + cols * 2, R)
+        4.0 * rows * cols * 2 + cols * 2)
     del xs, rs
     rows, cols = 8192, 14336
     g = rand_bf16((rows, cols), 22, std=2.0)
     u = rand_bf16((rows, cols), 23, std=2.0)
     out["silu_8192x14336"] = hbm_entry([lambda: aot_kernel.silu(g), lambda: aot_kernel.silu(u)],
-                                       2.0 * rows * cols * 2, 2)
+                                       2.0 * rows * cols * 2)
     out["silu_mul_8192x14336"] = hbm_entry([lambda: aot_kernel.silu_mul(g, u),
                                             lambda: aot_kernel.silu_mul(u, g)],
-                                           3.0 * rows * cols * 2, 2)
+                                           3.0 * rows * cols * 2)
     del g, u
     torch.cuda.empty_cache()
     return out
 
 
-def tp_mlp(args, rank: int, world: int, peaks: dict) -> dict:
-    import torch
-    import torch.distributed as dist
-
-    from aot_kernel.tp_mlp import (MLPShard, TensorParallelMLP, shard_down, shard_gate_up,
-                                   shard_gate_up_folded, shard_gate_up_interleaved)
-
-    T, H, inter = 4096, 8192, 28672
-    x = rand_bf16((T, H), 30)
-    nw = rand_bf16((H,), 31, std=0.1, mean=1.0)
-    w_gu = rand_bf16((H, 2 * inter), 32, std=0.02)
-    fused_silu = not args.tp_unfused_silu
-    fold_norm = fused_silu and not args.tp_unfolded_norm
-    if fold_norm:
-        wgu_r = shard_gate_up_folded(w_gu, nw, rank, world)
-    else:
-        wgu_r = (shard_gate_up_interleaved if fused_silu else shard_gate_up)(w_gu, rank, world)
-    del w_gu
-    w_d = rand_bf16((inter, H), 33, std=0.02)
-    wd_r = shard_down(w_d, rank, world)
-    del w_d
-    torch.cuda.empty_cache()
-    allreduce = args.tp_allreduce if world > 1 else "nccl"
-    block = TensorParallelMLP(MLPShard(nw, wgu_r, wd_r, fused_silu=fused_silu, fold_norm=fold_norm),
-                              eps=1e-6, chunks=args.tp_chunks, allreduce=allreduce)
-    for _ in range(max(3, args.warmup)):
-        block(x)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    steps = max(5, min(args.steps, 30))
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(steps):
-        block(x)
-    e.record()
-    torch.cuda.synchronize()
-    ms = torch.tensor([s.elapsed_time(e) / steps], device="cuda", dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms = float(ms.item())
-    phases = tp_phase_breakdown(block, x, world)
-    flops = 2.0 * T * H * 2 * inter + 2.0 * T * inter * H
-    per_gpu_ideal_ms = flops / world / (peaks["bf16_tflops"] * 1e12) * 1e3
-    return {"tokens_per_s": T / (ms * 1e-3), "ms_per_step": ms, "tokens": T, "hidden": H,
-            "intermediate": inter, "tp": world, "chunks": args.tp_chunks,
-            "allreduce": allreduce if world > 1 else None, "fused_silu": fused_silu,
-            "fold_norm": fold_norm,
-            "gpu_launches_per_step": (2 if fused_silu else 3)
-            + (1 if world == 1 or allreduce == "fused" else args.tp_chunks),
-            "tensor_frac_per_gpu": per_gpu_ideal_ms / ms, "allreduce_bytes": T * H * 2,
-            "phases_ms": phases}
-
-
-def tp_phase_breakdown(block, x, world: int, reps: int = 5) -> dict:
-    """Device time of each op of one block step (mean of `reps` passes outside
-    the timed region, CUDA events between ops, max over ranks).  A sleep
-    kernel queued first keeps the host ahead so dispatch gaps are not timed."""
-    import torch
-    import torch.distributed as dist
-
-    ops, s = block.ops, block.shard
-    fused = world > 1 and block.allreduce == "fused"
-    fsilu = s.fused_silu
-    if s.fold_norm:
-        names = ["rms_rstd", "gemm_gate_up+rms_norm+silu_mul (fused)"]
-    else:
-        names = ["rms_norm"] + (["gemm_gate_up+silu_mul (fused)"] if fsilu else
-                                ["gemm_gate_up", "silu_mul"])
-    names += ["gemm_down+all_reduce (fused)"] if fused else ["gemm_down", "all_reduce"]
-    acc = torch.zeros(len(names), dtype=torch.float64, device="cuda")
-    for _ in range(reps):
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        torch.cuda._sleep(2_000_000)
-        i = 0
-        ev[i].record()
-        if s.fold_norm:
-            rstd = ops.rms_rstd(x, block.eps)
-            i += 1
-            ev[i].record()
-            act = ops.gemm_silu_mul(x, s.w_gate_up, rstd)
-        elif fsilu:
-            h = ops.rms_norm(x, s.norm_weight, block.eps)
-            i += 1
-            ev[i].record()
-            act = ops.gemm_silu_mul(h, s.w_gate_up)
-        else:
-            h = ops.rms_norm(x, s.norm_weight, block.eps)
-            i += 1
-            ev[i].record()
-            gu = ops.gemm(h, s.w_gate_up)
-            i += 1
-            ev[i].record()
-            act = ops.silu_mul(gu[:, :block.inter_local], gu[:, block.inter_local:])
-        i += 1
-        ev[i].record()
-        if fused:
-            block._fused(act, s.w_down)
-        else:
-            out = ops.gemm(act, s.w_down)
-            i += 1
-            ev[i].record()
-            if world > 1:
-                dist.all_reduce(out)
-        i += 1
-        ev[i].record()
-        torch.cuda.synchronize()
-        acc += torch.tensor([ev[i].elapsed_time(ev[i + 1]) for i in range(len(names))],
-                            dtype=torch.float64, device="cuda")
-    acc /= reps
-    if world > 1:
-        dist.all_reduce(acc, op=dist.ReduceOp.MAX)
-    return {n: round(v, 4) for n, v in zip(names, acc.tolist())}
-
-
-def cpu_baseline(target_s: float = 8.0) -> dict:
-    """The reference's CPU GEMM on a bounded row sample of the 8192^3 problem.
-
-    ``ref.gemm`` is ``a @ b`` (ref/gemm.py:4-5); on CPU bf16 tensors torch runs
-    it through its own bf16 GEMM with every host thread.  That call, ported
-    as one line, is the timed value.  The numpy oracle (float32 BLAS) is timed
-    beside it for reference.
-    """
-    import torch
-
-    from oracle import ops
-
-    M, N, K = HEADLINE
-    rows = 1024
-    torch.set_num_threads(os.cpu_count() or 1)
-    g = torch.Generator().manual_seed(0)
-    a = torch.randn((rows, K), generator=g).to(torch.bfloat16)
-    b = (torch.randn((K, N), generator=g) * K ** -0.5).to(torch.bfloat16)
-
-    def timed(fn, budget):
-        fn()  # warm thread pools / packing
-        n, t0 = 0, time.perf_counter()
-        while True:
-            fn()
-            n += 1
-            el = time.perf_counter() - t0
-            if el >= budget or n >= 500:
-                return n, el
-
-    n, el = timed(lambda: a @ b, target_s)
-    a_np, b_np = a.float().numpy(), b.float().numpy()
-    n_np, el_np = timed(lambda: ops.gemm(a_np, b_np, "bfloat16"), target_s / 2)
-    flops = 2.0 * rows * N * K
-    return {"value": flops * n / el / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
-            "kind": "port",
-            "sample": f"A[{rows} of {M} rows, {K}] @ B[{K},{N}] bf16 on CPU via torch (the call "
-                      f"ref.gemm makes), {n} repetitions in {el:.1f} s",
-            "oracle_numpy_tflops": flops * n_np / el_np / 1e12,
-            "cpu_count": os.cpu_count()}
-
-
 # ---------------------------------------------------------------- main
 
 def base_line(args, world: int) -> dict:
-    M, N, K = HEADLINE
     return {
-        "metric": "bf16 GEMM TFLOP/s (M=N=K=8192, fp32 accumulate, bf16 out)",
-        "unit": "TFLOP/s",
+        "metric": "TP MLP tokens/s (Llama-3-70B MLP block, 4096 tokens, bf16)",
+        "unit": "tokens/s",
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic: seeded A ~ N(0,1), B ~ N(0,1/K) (Philox on device)",
-        "config": {"workload": "square bf16 GEMM C[8192,8192] = A[8192,8192] B[8192,8192]",
-                   "M": M, "N": N, "K": K,
-                   "parallelism": f"replicas x{world} (one independent GEMM per GPU)",
-                   "l2": "operands 256 MB > 126 MB L2 (no reuse across steps)"},
+        "data": "synthetic: seeded x ~ N(0,1), norm weight N(1,0.1), weights N(0,0.02)",
+        "config": {"workload": "Llama-3-70B MLP block: x[4096,8192] -> rms_norm -> gate/up "
+                               "8192->2x28672 -> silu(gate)*up -> down 28672->8192 -> all-reduce",
+                   "tokens": TOKENS, "hidden": HIDDEN, "intermediate": INTER,
+                   "l2": "weights 1.41 GB split over the ranks plus activations exceed the 126 MB "
+                         "L2; every step re-reads them"},
     }
 
 
 def run_reference(args) -> None:
+    """The reference composition on the host's cores, rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    cb = None
-    per_step = []
-    for i in range(args.warmup + args.steps):
-        r = cpu_baseline(target_s=1.0)
-        if i >= args.warmup:
-            per_step.append(r)
-        cb = r
-    value = statistics.mean(r["value"] for r in per_step)
-    line = base_line(args, int(os.environ.get("WORLD_SIZE", "1")))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    x, nw, wgu, wd = _cpu_inputs()
+    times, cores = cpu_block_times(x, nw, wgu, wd, steps=args.steps, warmup=args.warmup)
+    mean = statistics.mean(times)
+    value = TOKENS / mean
+    line = base_line(args, world)
     line.update({
-        "impl": "reference", "value": value,
-        "ms_per_step": statistics.mean(2.0 * 1024 * 8192 * 8192 / (r["value"] * 1e12) * 1e3
-                                       for r in per_step),
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cb["cores"], "kind": "port",
-                         "sample": cb["sample"]},
-        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "impl": "reference", "parallelism": "host CPU, all threads (one process)",
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"the full block (4096 tokens) x {len(times)} timed steps after "
+                                   f"{args.warmup} warm-up; torch CPU composition of ref.rmsnorm, "
+                                   f"ref.gemm, ref.silu"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
+        "value": value, "ms_per_step": mean * 1e3,
     })
-    line["config"]["parallelism"] = "host CPU, all threads (ref.gemm = a @ b on CPU tensors)"
     print(json.dumps(line), flush=True)
 
 
@@ -688,6 +706,7 @@ def run_case(args) -> None:
     import torch
 
     import aot_kernel
+    from aot_kernel import capi
 
     kind, shape = CASES[args.case]
     if kind == "gemm":
@@ -695,11 +714,23 @@ def run_case(args) -> None:
         a = rand_bf16((M, K), 1)
         b = rand_bf16((K, N), 2, std=0.02)
         fn = lambda: aot_kernel.gemm(a, b)  # noqa: E731
+    elif kind == "gemm_tc2":
+        M, K, N = shape
+        a = rand_bf16((M, K), 1)
+        b = rand_bf16((K, N), 2, std=0.02)
+        c = torch.empty((M, N), device="cuda", dtype=torch.bfloat16)
+        fn = lambda: capi.gemm_tc2(c, a, b, M, N, K, capi.dtype_code(a.dtype))  # noqa: E731
     elif kind == "gate_up_silu":
         M, K, inter = shape
         a = rand_bf16((M, K), 1)
         w = rand_bf16((K, 2 * inter), 2, std=0.02)
         fn = lambda: aot_kernel.gemm_silu_mul(a, w)  # noqa: E731
+    elif kind == "tp_gate_up":
+        M, K, inter = shape
+        a = rand_bf16((M, K), 1)
+        w = rand_bf16((K, 2 * inter), 2, std=0.02)
+        rstd = aot_kernel.rms_rstd(a)
+        fn = lambda: aot_kernel.gemm_silu_mul(a, w, rstd)  # noqa: E731
     elif kind.startswith("scaled_gemm"):
         M, K, N = shape
         q = kind.rsplit("_", 1)[1]
@@ -710,6 +741,9 @@ def run_case(args) -> None:
         x = rand_bf16(shape, 3)
         w = rand_bf16((shape[1],), 4, std=0.1, mean=1.0)
         fn = lambda: aot_kernel.rms_norm(x, w)  # noqa: E731
+    elif kind == "rms_rstd":
+        x = rand_bf16(shape, 3)
+        fn = lambda: aot_kernel.rms_rstd(x)  # noqa: E731
     elif kind == "add_rms_norm":
         x = rand_bf16(shape, 3)
         r = rand_bf16(shape, 8)
@@ -727,6 +761,46 @@ def run_case(args) -> None:
     torch.cuda.synchronize()
 
 
+def run_ours(args, rank: int, world: int, local: int, guard, held: dict) -> dict:
+    import torch
+
+    from aot_kernel import capi
+
+    peaks, peak_src = load_peaks()
+    x, block, host = tp_build(args, rank, world)
+    held["block"] = block
+    head = tp_timed(args, block, x, world, peaks, guard)
+    head["roofline"]["peak_source"] = f"{peak_src} (burst bf16 GEMM)"
+    guard.check()
+    e2e = tp_e2e(args, block, x, rank, world, guard)
+    guard.check()
+    parity = tp_parity(block, x, host, rank)
+    line = base_line(args, world)
+    line["parallelism"] = (f"tp{world}: column-split gate/up, row-split down, "
+                           + ("down GEMM fused with an NVSwitch all-reduce" if world > 1 and
+                              block.allreduce == "fused" else
+                              "NCCL all-reduce" if world > 1 else "one GPU"))
+    line["phases_ms"] = head["phases_ms"]
+    line["tensor_frac_per_gpu"] = round(BLOCK_FLOPS / world / (peaks["bf16_tflops"] * 1e12)
+                                        / (head["ms_per_step"] * 1e-3), 4)
+    if rank == 0 and world == 1 and not args.no_kernels:
+        del block, held["block"]
+        gc.collect()
+        torch.cuda.empty_cache()
+        line["kernels_fields"] = "[ms, TFLOP/s or GB/s, fraction of the measured peak]"
+        line["kernels"] = kernel_table(peaks)
+        line["gemm_8192"] = gemm_8192(args, peaks)
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(host)
+    wd = capi.watchdog_status(local)
+    if wd:
+        line["watchdog"] = wd
+    line.update({k: head[k] for k in ("gpu_launches", "clocks", "value", "ms_per_step", "roofline")})
+    line["e2e"] = e2e
+    line["tp_parity"] = parity
+    return line
+
+
 def main() -> None:
     args = parse_args()
     if args.impl == "reference":
@@ -735,6 +809,9 @@ def main() -> None:
     if args.case:
         run_case(args)
         return
+    from aot_kernel.rank_guard import RankGuard, nccl_env
+
+    nccl_env(blocking=False)
     import torch
     import torch.distributed as dist
 
@@ -743,33 +820,36 @@ def main() -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
+        store = dist.distributed_c10d._get_default_store()
+    else:
+        store = dist.HashStore()
     import aot_kernel  # noqa: F401  (fails loudly when the extension is missing)
-    from aot_kernel import capi
 
-    peaks, peak_src = load_peaks()
-    line = base_line(args, world)
-    head = headline_gemm(args, rank, world, peaks)
-    line.update({k: head[k] for k in ("value", "ms_per_step", "roofline", "e2e", "gpu_launches",
-                                      "clocks")})
-    line["roofline"]["peak_source"] = f"{peak_src} (burst bf16 GEMM)"
-    if not args.no_tp:
-        line["tp_mlp"] = tp_mlp(args, rank, world, peaks)
-    if rank == 0 and world == 1 and not args.no_kernels:
-        line["kernels"] = kernel_table(peaks)
-        line["kernels"]["peaks"] = {"hbm_gbs": peaks["hbm_gbs"], "bf16_tflops": peaks["bf16_tflops"],
-                                    "source": peak_src}
-    if rank == 0 and world == 1 and not args.no_cpu:
-        line["cpu_baseline"] = cpu_baseline()
-    wd = capi.watchdog_status(local)
-    if wd:
-        line["watchdog"] = wd
-    if world > 1:
-        dist.barrier()
+    guard = RankGuard(store, rank, world, prefix="bench")
+    held: dict = {}
+    line, ok = None, False
+    try:
+        line = run_ours(args, rank, world, local, guard, held)
+        ok = True
+    except BaseException:  # noqa: BLE001  (reported below; the rank leaves through the guard)
+        traceback.print_exc()
+
+    def release():
+        held.clear()
+        gc.collect()
+        torch.cuda.synchronize()
+
+    clean = guard.finish(ok, release, sync=torch.cuda.synchronize)
+    if world > 1 and clean:
         dist.destroy_process_group()
-    if rank == 0:
+    if rank == 0 and clean and line is not None:
         print(json.dumps(line), flush=True)
+    sys.stdout.flush()
+    if not clean:
+        sys.stderr.flush()
+        os._exit(1)
 
 
 if __name__ == "__main__":

@@ -30,12 +30,17 @@ from datetime import timedelta
 from typing import Callable
 
 
-def nccl_env() -> None:
-    """Makes NCCL collectives raise on their timeout instead of aborting the
-    process: blocking waits, no asynchronous teardown.  Call before the
-    process group is created."""
-    os.environ.setdefault("TORCH_NCCL_BLOCKING_WAIT", "1")
-    os.environ.setdefault("TORCH_NCCL_ASYNC_ERROR_HANDLING", "0")
+def nccl_env(blocking: bool = True) -> None:
+    """Makes a timed-out NCCL collective come back as an error instead of
+    tearing the process down: with ``blocking`` every wait blocks the host
+    and raises on the timeout; without it (for code that overlaps collectives
+    with other streams) the timed-out communicator is aborted and later calls
+    raise.  Call before the process group is created."""
+    if blocking:
+        os.environ.setdefault("TORCH_NCCL_BLOCKING_WAIT", "1")
+        os.environ.setdefault("TORCH_NCCL_ASYNC_ERROR_HANDLING", "0")
+    else:
+        os.environ.setdefault("TORCH_NCCL_ASYNC_ERROR_HANDLING", "2")
 
 
 class PeerFailed(RuntimeError):

@@ -160,20 +160,42 @@ class TensorParallelMLP:
             raise ValueError("fold_norm needs the fused gate/up + silu layout (fused_silu=True)")
         self._fused: FusedDownAllReduce | None = None
 
-    def gate_up_act(self, x: torch.Tensor) -> torch.Tensor:
-        """rms_norm, gate/up projection and silu(gate) * up of one step."""
+    def gate_up_act(self, x: torch.Tensor, gate_up_events=None) -> torch.Tensor:
+        """rms_norm, gate/up projection and silu(gate) * up of one step.
+        ``gate_up_events`` (a pair of CUDA events) is recorded on the current
+        stream around the gate/up GEMM launch, for timing that kernel alone."""
         ops, s = self.ops, self.shard
+        ev = gate_up_events or ()
+
+        def mark(i):
+            if ev:
+                ev[i].record()
+
         if s.fold_norm:
-            return ops.gemm_silu_mul(x, s.w_gate_up, ops.rms_rstd(x, self.eps))
+            rstd = ops.rms_rstd(x, self.eps)
+            mark(0)
+            act = ops.gemm_silu_mul(x, s.w_gate_up, rstd)
+            mark(1)
+            return act
         h = ops.rms_norm(x, s.norm_weight, self.eps)
+        mark(0)
         if s.fused_silu:
-            return ops.gemm_silu_mul(h, s.w_gate_up)
+            act = ops.gemm_silu_mul(h, s.w_gate_up)
+            mark(1)
+            return act
         gu = ops.gemm(h, s.w_gate_up)
+        mark(1)
         return ops.silu_mul(gu[:, :self.inter_local], gu[:, self.inter_local:])
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def launches_per_step(self) -> int:
+        """Kernels one ``forward`` launches (NCCL's all-reduce kernels not counted)."""
+        s = self.shard
+        n = 2 if s.fused_silu else 3          # rms_norm / rms_rstd, gate/up (+ silu_mul)
+        return n + (self.chunks if self.world > 1 and self.allreduce == "nccl" else 1)
+
+    def forward(self, x: torch.Tensor, gate_up_events=None) -> torch.Tensor:
         ops, s = self.ops, self.shard
-        act = self.gate_up_act(x)
+        act = self.gate_up_act(x, gate_up_events)
         if self.world == 1:
             return ops.gemm(act, s.w_down)
         if self.allreduce == "fused":
@@ -200,3 +222,84 @@ class TensorParallelMLP:
         return out
 
     __call__ = forward
+
+
+class HostStream:
+    """Runs a ``TensorParallelMLP`` on batches that live in pinned HOST memory,
+    the way a serving loop feeds it: ``submit(x_host, out_host)`` enqueues one
+    batch and returns; batch i+1's copy-in and batch i-1's copy-out run on
+    their own streams while batch i's kernels run.
+
+    Over W ranks the host link carries every input row once: rank r copies
+    rows [r*T/W, (r+1)*T/W) of ``x_host`` in, the ranks all-gather x over
+    NVLink (NCCL, on a side stream), the block runs, and rank r copies the
+    same rows of the (all-reduced, replicated) output back into ``out_host``,
+    so the W ranks' host buffers together hold the whole result.  Two device
+    slots per rank; a slot is reused only after the batch that used it has
+    been read back.
+    """
+
+    def __init__(self, block: TensorParallelMLP, tokens: int, hidden: int, device,
+                 dtype=torch.bfloat16, group=None, slots: int = 2):
+        self.block, self.group = block, group
+        self.world = block.world
+        self.rank = dist.get_rank(group) if self.world > 1 else 0
+        if tokens % self.world:
+            raise ValueError(f"{tokens} tokens do not split over {self.world} ranks")
+        rows = tokens // self.world
+        self.lo, self.hi = self.rank * rows, (self.rank + 1) * rows
+        self.shape = (tokens, hidden)
+        self.slots = slots
+        self.x = [torch.empty((tokens, hidden), dtype=dtype, device=device) for _ in range(slots)]
+        self.xin = [self.x[i][self.lo:self.hi] if self.world == 1 else
+                    torch.empty((rows, hidden), dtype=dtype, device=device) for i in range(slots)]
+        self.stage = [torch.empty((rows, hidden), dtype=dtype, device=device) for _ in range(slots)]
+        self.h2d = torch.cuda.Stream(device)
+        self.d2h = torch.cuda.Stream(device)
+        self.gather = torch.cuda.Stream(device) if self.world > 1 else None
+        self.x_free = [torch.cuda.Event() for _ in range(slots)]
+        self.stage_free = [torch.cuda.Event() for _ in range(slots)]
+        self.n = 0
+
+    def h2d_bytes(self) -> int:
+        return self.xin[0].nbytes
+
+    def d2h_bytes(self) -> int:
+        return self.stage[0].nbytes
+
+    def submit(self, x_host: torch.Tensor, out_host: torch.Tensor) -> None:
+        if tuple(x_host.shape) != self.shape or tuple(out_host.shape) != self.shape:
+            raise ValueError(f"host batches must be {list(self.shape)}")
+        if x_host.device.type != "cpu" or out_host.device.type != "cpu":
+            raise ValueError("submit takes host tensors (pinned for asynchronous copies)")
+        s = self.n % self.slots
+        cur = torch.cuda.current_stream()
+        with torch.cuda.stream(self.h2d):
+            if self.n >= self.slots:
+                self.h2d.wait_event(self.x_free[s])
+            self.xin[s].copy_(x_host[self.lo:self.hi], non_blocking=True)
+            landed = torch.cuda.Event()
+            landed.record(self.h2d)
+        if self.world > 1:
+            self.gather.wait_event(landed)
+            with torch.cuda.stream(self.gather):
+                dist.all_gather_into_tensor(self.x[s], self.xin[s], group=self.group)
+            cur.wait_stream(self.gather)
+        else:
+            cur.wait_event(landed)
+        y = self.block(self.x[s])
+        self.x_free[s].record(cur)
+        if self.n >= self.slots:
+            cur.wait_event(self.stage_free[s])
+        self.stage[s].copy_(y[self.lo:self.hi])
+        staged = torch.cuda.Event()
+        staged.record(cur)
+        with torch.cuda.stream(self.d2h):
+            self.d2h.wait_event(staged)
+            out_host[self.lo:self.hi].copy_(self.stage[s], non_blocking=True)
+            self.stage_free[s].record(self.d2h)
+        self.n += 1
+
+    def drain(self) -> None:
+        """Makes the current stream wait for every submitted batch's copy-out."""
+        torch.cuda.current_stream().wait_stream(self.d2h)
