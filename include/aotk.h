@@ -148,8 +148,8 @@ AOTK_API int aotk_gemm_opt_workspace_size(int64_t M, int64_t N, int64_t K, int d
  * where the library's kernels are loaded until the process exits).  The
  * entry point calls no cudaMalloc, cudaFree or allocating library routine.
  * The first call on a device looks up the array's device address
- * (cudaGetSymbolAddress, once per device); make that first call before any
- * stream capture.  Every call on a device shares the one array and resets the
+ * (cudaGetSymbolAddress; kept once it succeeds, retried while it fails);
+ * make that first call before any stream capture.  Every call on a device shares the one array and resets the
  * part it needs, so calls whose kernels overlap on the GPU (different streams
  * without ordering) race and corrupt each other's results; order them on one
  * stream.  Problems needing more scratch than the array holds return

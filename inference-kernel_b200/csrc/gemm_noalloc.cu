@@ -13,7 +13,7 @@
 // exits.  Host code must not hand the symbol itself to a kernel: on the host
 // the name only stands for the variable.  Its device address is looked up
 // once per device with cudaGetSymbolAddress, with that device current, the
-// first time the entry point runs on it.
+// first time the entry point runs on it (retried until a lookup succeeds).
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -31,22 +31,26 @@ namespace aotk {
 namespace {
 
 constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
 void* g_scratch_ptr[kMaxDevices] = {};
-std::once_flag g_scratch_once[kMaxDevices];
-cudaError_t g_scratch_err[kMaxDevices] = {};
 
-// Device address of g_static_scratch on the current device (looked up once).
+// Device address of g_static_scratch on the current device.  Only a
+// successful lookup is cached: a lookup that failed (inside a stream capture,
+// say, or on a transient driver error) is retried on the next call.
 int static_scratch(int device, void** ptr) {
   if (device < 0 || device >= kMaxDevices)
     return fail(AOTK_ERR_CUDA, "device ordinal %d out of range", device);
-  std::call_once(g_scratch_once[device], [device] {
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_ptr[device] == nullptr) {
     void* p = nullptr;
-    g_scratch_err[device] = cudaGetSymbolAddress(&p, g_static_scratch);
+    cudaError_t err = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (err != cudaSuccess || p == nullptr) {
+      if (err != cudaSuccess) cudaGetLastError();  // not sticky: leave no error behind
+      return fail(AOTK_ERR_CUDA, "cudaGetSymbolAddress(static scratch) on device %d: %s", device,
+                  cudaGetErrorString(err));
+    }
     g_scratch_ptr[device] = p;
-  });
-  if (g_scratch_err[device] != cudaSuccess || g_scratch_ptr[device] == nullptr)
-    return fail(AOTK_ERR_CUDA, "cudaGetSymbolAddress(static scratch) on device %d: %s", device,
-                cudaGetErrorString(g_scratch_err[device]));
+  }
   *ptr = g_scratch_ptr[device];
   return AOTK_OK;
 }

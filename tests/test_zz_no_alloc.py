@@ -46,3 +46,25 @@ def test_noalloc_matches_workspace_entry_point(shape):
         assert torch.equal(c, ref)  # same schedule, deterministic split order
     assert capi.watchdog_status() == 0
 
+
+def test_noalloc_takes_no_device_memory():
+    """After a first call (which only looks up the static array's address),
+    further calls leave the device's free memory exactly where it was."""
+    import torch
+
+    from aot_kernel import capi
+
+    M, K, N = SHAPES[0]
+    a = to_device(randn((M, K), 910, "bfloat16"), "bfloat16")
+    b = to_device(randn((K, N), 911, "bfloat16", std=K ** -0.5), "bfloat16")
+    c = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    capi.gemm_opt_noalloc(c, a, b, M, N, K, capi.BFLOAT16)
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        capi.gemm_opt_noalloc(c, a, b, M, N, K, capi.BFLOAT16)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+    assert capi.watchdog_status() == 0
+
