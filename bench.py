@@ -303,14 +303,16 @@ def tp_timed(args, block, x, world: int, peaks: dict, guard) -> dict:
 
     for _ in range(args.warmup):
         block(x)
-    _meet(world)
-    guard.check()
 
     def ev():
         return torch.cuda.Event(enable_timing=True)
 
+    # The sampler starts (NVML set-up can take a second) before the ranks
+    # meet, so that every rank enters the timed steps at the same moment.
     with ClockSampler(torch.cuda.current_device()) as clocks:
         evs = [(ev(), ev(), ev(), ev()) for _ in range(args.steps)]
+        _meet(world)
+        guard.check()
         t0, t1 = ev(), ev()
         t0.record()
         for a, b, c, d in evs:

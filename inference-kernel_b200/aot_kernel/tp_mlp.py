@@ -232,7 +232,7 @@ class HostStream:
 
     Over W ranks the host link carries every input row once: rank r copies
     rows [r*T/W, (r+1)*T/W) of ``x_host`` in, the ranks all-gather x over
-    NVLink (NCCL, on a side stream), the block runs, and rank r copies the
+    NVLink (NCCL, on the block's stream), the block runs, and rank r copies the
     same rows of the (all-reduced, replicated) output back into ``out_host``,
     so the W ranks' host buffers together hold the whole result.  Two device
     slots per rank; a slot is reused only after the batch that used it has
@@ -256,7 +256,6 @@ class HostStream:
         self.stage = [torch.empty((rows, hidden), dtype=dtype, device=device) for _ in range(slots)]
         self.h2d = torch.cuda.Stream(device)
         self.d2h = torch.cuda.Stream(device)
-        self.gather = torch.cuda.Stream(device) if self.world > 1 else None
         self.x_free = [torch.cuda.Event() for _ in range(slots)]
         self.stage_free = [torch.cuda.Event() for _ in range(slots)]
         self.n = 0
@@ -280,13 +279,13 @@ class HostStream:
             self.xin[s].copy_(x_host[self.lo:self.hi], non_blocking=True)
             landed = torch.cuda.Event()
             landed.record(self.h2d)
+        cur.wait_event(landed)
         if self.world > 1:
-            self.gather.wait_event(landed)
-            with torch.cuda.stream(self.gather):
-                dist.all_gather_into_tensor(self.x[s], self.xin[s], group=self.group)
-            cur.wait_stream(self.gather)
-        else:
-            cur.wait_event(landed)
+            # On the block's own stream, never beside it: the fused down
+            # GEMM + all-reduce needs all its CTAs resident at once, and an
+            # NCCL kernel that held SMs while waiting for a peer (whose own
+            # fused kernel waits for this rank) would deadlock the two.
+            dist.all_gather_into_tensor(self.x[s], self.xin[s], group=self.group)
         y = self.block(self.x[s])
         self.x_free[s].record(cur)
         if self.n >= self.slots:

@@ -53,7 +53,16 @@ __device__ unsigned g_tc_watchdog;
 constexpr int kBM = 128;
 constexpr int kThreads = 192;       // plain GEMM: producer, MMA, 4 epilogue warps
 constexpr int kThreadsFused = 320;  // + 4 all-reduce warps (gemm_allreduce)
-constexpr int kGroupM = 16;  // M tiles per raster group
+#ifndef AOTK_TC_GROUP_M
+#define AOTK_TC_GROUP_M 16
+#endif
+#ifndef AOTK_TC_A_POLICY
+#define AOTK_TC_A_POLICY 0  // 0: default, 1: evict_last
+#endif
+#ifndef AOTK_TC_B_POLICY
+#define AOTK_TC_B_POLICY 0  // 0: default, 1: evict_first, 2: evict_last
+#endif
+constexpr int kGroupM = AOTK_TC_GROUP_M;  // M tiles per raster group
 constexpr int kMaxSplits = 4;
 // K blocks below which a K split does not pay for its partial-tile traffic
 // (measured on B200: a 4-way split of 64 K blocks lost to whole tiles, of 128
@@ -255,15 +264,16 @@ __device__ __forceinline__ void st_global_v4(float* p, uint32_t a, uint32_t b, u
 
 // Fused all-reduce of the output over W ranks (one process per GPU) through
 // NVSwitch multicast memory.  Each rank stores its partial tile into its own
-// `part` buffer, then bumps the tile's arrival counter on the owner rank
-// (tile_owner: rotates over the ranks from round to round).  The owner's
-// all-reduce warps wait until all W partials of the tile have arrived, read
-// their sum through the multicast address of `part`
-// (multimem.ld_reduce, fp32 accumulation) and write it to every rank's `out`
-// through the multicast address of `out` (multimem.st).  Counters only grow:
-// call number e (epoch, from 1) waits for W*e arrivals.  A final done
-// counter per rank (W * grid * e) tells each rank when every owner has
-// written its tiles.
+// `part` buffer, then bumps the tile's arrival counter on every rank.  Every
+// rank reduces a 1/W slice of the rows of every tile it computed: once all W
+// partials of the tile have arrived, its all-reduce warps read the slice's
+// sum through the multicast address of `part` (multimem.ld_reduce, fp32
+// accumulation) and write it to every rank's `out` through the multicast
+// address of `out` (multimem.st).  So in every round of tiles every CTA of
+// every rank has reduction work, and the last round's tiles are reduced by
+// all W ranks at once.  Counters only grow: call number e (epoch, from 1)
+// waits for W*e arrivals.  A final done counter per rank (W * grid * e) tells
+// each rank when every rank has written its slices.
 struct ArParams {
   int rank, world;
   uint64_t part_mc, out_mc;        // multicast addresses of part / out
@@ -289,24 +299,29 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-// Owner rank of a tile: rotates with the round so that every CTA reduces about
-// 1/W of the tiles it computes (tile = cta + round * grid on every rank).
-__device__ __forceinline__ int tile_owner(int tile, int world) {
-  return (tile % gridDim.x + tile / gridDim.x) % world;
-}
-
 __device__ __forceinline__ void comm_bar_sync() {
   asm volatile("bar.sync 2, 128;" ::: "memory");  // warps 6..9 only
 }
-// Waits until *p >= target; bounded like the pipeline waits (on a timeout:
-// raises *abort, ORs `code` into *status and returns false).
+// Waits until *p >= target, which a peer rank's kernel raises.  Ranks are
+// separate host processes whose launches can drift apart by far more than
+// the ~1 s a pipeline wait allows (interpreter pauses, first-call set-up), so
+// cross-rank waits are bounded in wall time (%globaltimer) at 10 s instead;
+// only a peer that never arrives ends one.  On a timeout: raises *abort, ORs
+// `code` into *status and returns false.
+constexpr unsigned long long kPeerWaitLimitNs = 10000000000ull;
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 __device__ __forceinline__ bool wait_at_least(const unsigned* p, unsigned target,
                                               volatile int* abort, unsigned* status,
                                               unsigned code = kWdPeer) {
-  const long long t0 = clock64();
+  if (static_cast<int>(ld_acquire_sys(p) - target) >= 0) return true;
+  const unsigned long long t0 = globaltimer_ns();
   while (static_cast<int>(ld_acquire_sys(p) - target) < 0) {
     if (*abort) return false;
-    if (clock64() - t0 > kWaitLimitCycles) {
+    if (globaltimer_ns() - t0 > kPeerWaitLimitNs) {
       *abort = 1;
       atomicOr(status, code);
       return false;
@@ -443,6 +458,22 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
+#if AOTK_TC_A_POLICY == 1
+      const uint64_t a_pol = l2_policy_evict_last();
+      auto load_a = [&](uint32_t dst, int x, int y, uint32_t bar) {
+        tma_load_2d_hint(dst, &tmA, x, y, bar, a_pol);
+      };
+#else
+      auto load_a = [&](uint32_t dst, int x, int y, uint32_t bar) { tma_load_2d(dst, &tmA, x, y, bar); };
+#endif
+#if AOTK_TC_B_POLICY == 1 || AOTK_TC_B_POLICY == 2
+      const uint64_t b_pol = AOTK_TC_B_POLICY == 1 ? l2_policy_evict_first() : l2_policy_evict_last();
+      auto load_b = [&](uint32_t dst, int x, int y, uint32_t bar) {
+        tma_load_2d_hint(dst, &tmB, x, y, bar, b_pol);
+      };
+#else
+      auto load_b = [&](uint32_t dst, int x, int y, uint32_t bar) { tma_load_2d(dst, &tmB, x, y, bar); };
+#endif
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
@@ -459,19 +490,18 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
           }
           const uint32_t fb = full_bar(stage);
           mbar_arrive_expect_tx(fb, L::kABytes + nbox * L::kBBox);
-          tma_load_2d(sA + stage * L::kABytes, &tmA, kb * kBK, mb * kBM, fb);
+          load_a(sA + stage * L::kABytes, kb * kBK, mb * kBM, fb);
           // Straight-line issue (constant trip counts): a runtime loop here
           // cost 8 % of whole-tile throughput on B200.
           if (w.half < 0) {
 #pragma unroll
             for (int j = 0; j < BN / L::kBoxN; ++j)
-              tma_load_2d(sB + stage * L::kBBytes + j * L::kBBox, &tmB, nb * BN + j * L::kBoxN,
-                          kb * kBK, fb);
+              load_b(sB + stage * L::kBBytes + j * L::kBBox, nb * BN + j * L::kBoxN, kb * kBK, fb);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 2 / L::kBoxN; ++j)
-              tma_load_2d(sB + stage * L::kBBytes + j * L::kBBox, &tmB,
-                          b_box_col<BN, L::kBoxN, kSiluMul>(nb, w.half, j), kb * kBK, fb);
+              load_b(sB + stage * L::kBBytes + j * L::kBBox,
+                     b_box_col<BN, L::kBoxN, kSiluMul>(nb, w.half, j), kb * kBK, fb);
           }
           ++issued;
           if (++stage == STAGES) {
@@ -781,14 +811,14 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
       }
       if constexpr (kFused) {
         // The partial tile is in `part` once this warp's stores complete;
-        // after all four epilogue warps, count it in on the tile's owner.
+        // after all four epilogue warps, count it in on every rank.
         if (lane == 0) bulk_wait_all();
         __syncwarp();
         fence_proxy_async_global();
         fence_sys();
         epilogue_bar_sync();
         if (warp == 2 && lane == 0)
-          red_release_sys_add(ar.peer_counters[tile_owner(w.tile, ar.world)] + w.tile, 1u);
+          for (int p = 0; p < ar.world; ++p) red_release_sys_add(ar.peer_counters[p] + w.tile, 1u);
       }
       if (++acc == 2) {
         acc = 0;
@@ -799,14 +829,17 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
     __syncwarp();
   } else if constexpr (kFused) {
     // ---------------- all-reduce (warps 6..9) ----------------
-    // Same work list as the epilogue; for each tile this rank owns, wait for
-    // all W partials, then reduce through the switch and broadcast the sum.
+    // Same work list as the epilogue; for each tile, wait for all W partials,
+    // then reduce this rank's slice of its rows through the switch and
+    // broadcast the sum.
     const int ct = threadIdx.x - 192;  // 0..127
     volatile int* peer_ok = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 12);
     constexpr int kVecPerRow = BN * 2 / 16;
+    const int slice_rows = (kBM + ar.world - 1) / ar.world;
+    const int row0 = ar.rank * slice_rows;
+    const int nvec = max(0, min(kBM, row0 + slice_rows) - row0) * kVecPerRow;
     WorkItem w;
     for (int i = 0; work_item(sched, i, w); ++i) {
-      if (tile_owner(w.tile, ar.world) != ar.rank) continue;
       if (ct == 0)
         *peer_ok = wait_at_least(ar.counters + w.tile, ar.epoch * ar.world, abort_flag, wd) ? 1 : 0;
       comm_bar_sync();
@@ -817,16 +850,17 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
       tile_coords(w.tile, tiles_m, tiles_n, mb, nb);
       constexpr int kInFlight = 8;  // 16-byte reductions per thread in flight
 #pragma unroll 1
-      for (int v0 = ct; v0 < kBM * kVecPerRow; v0 += kInFlight * 128) {
+      for (int v0 = ct; v0 < nvec; v0 += kInFlight * 128) {
         uint4 val[kInFlight];
         uint64_t off[kInFlight];
         bool live[kInFlight];
 #pragma unroll
         for (int u = 0; u < kInFlight; ++u) {
           const int v = v0 + u * 128;
-          const int gr = mb * kBM + v / kVecPerRow;
+          const int gr = mb * kBM + row0 + v / kVecPerRow;
           const int gc = nb * BN + (v % kVecPerRow) * 8;
-          live[u] = gr < M && gc < N;  // N % 8 == 0: the whole 16-byte vector is in range
+          // N % 8 == 0: a 16-byte vector is all in range or all out
+          live[u] = v < nvec && gr < M && gc < N;
           off[u] = (static_cast<uint64_t>(gr) * N + gc) * sizeof(T);
           if (live[u]) {
             if constexpr (sizeof(T) == 2 && std::is_same<T, __nv_bfloat16>::value)
@@ -840,7 +874,7 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
           if (live[u]) multimem_st16(ar.out_mc + off[u], val[u]);
       }
     }
-    // Every owner on every rank has written its tiles once all W * grid CTAs
+    // Every rank has written its slices of every tile once all W * grid CTAs
     // have checked in on this rank.
     fence_sys();
     comm_bar_sync();
@@ -860,8 +894,9 @@ __global__ void __launch_bounds__(kEpi == kEpiAllReduce ? kThreadsFused : kThrea
 }
 
 // Exercises the bounded waits with nothing to wait for: an mbarrier phase that
-// no thread or copy completes, then a flag that nothing sets.  Each gives up
-// after kWaitLimitCycles and records its watchdog bit; the kernel returns.
+// no thread or copy completes (gives up after kWaitLimitCycles, ~1 s), then a
+// flag that nothing sets (gives up after kPeerWaitLimitNs, 10 s).  Each
+// records its watchdog bit; the kernel returns.
 __global__ void watchdog_selftest_kernel() {
   __shared__ __align__(8) uint64_t bar;
   __shared__ int abort_flag;
