@@ -302,27 +302,20 @@ int launch_skinny(void* c, const void* a, const void* b, int M, int N, int K, bo
   const int ntiles = (N + kTileN - 1) / kTileN;
   const int kblocks = (K + kBK - 1) / kBK;
   // One wave: every CTA streams an equal share of the weight at the same time.
-  // For 16-32 activation rows the split fills one CTA per SM (S = SMs /
-  // strips): more, shorter K slices cost more in pipeline fill and cluster
-  // reduction than they gain.  For 64-128 rows, whose CTAs also stream the
-  // activation tile and run full-height MMAs, the split is the largest
-  // cluster size whose `ntiles` clusters are all resident at once - two CTAs
-  // per SM (measured on B200: M = 128 x K = 14336 x N = 4096 32.3 -> 27.8 us,
-  // while M = 1 lost 5 % that way).
+  // The split is the largest cluster size (<= 8, <= K blocks) whose `ntiles`
+  // clusters are all resident at once - up to two CTAs per SM - so that the
+  // most weight bytes are in flight from the first K block on.  Measured on
+  // B200 (graph-free back-to-back launches): M = 1 x K = 4096 x N = 6144
+  // 13.0 -> 11.1 us against one CTA per SM (S = SMs / strips); M = 128 x
+  // K = 14336 x N = 4096 32.3 -> 27.8 us against S = SMs / strips.  Larger
+  // clusters that do not fit in one wave lose up to 2x.
   int S = 1;
-  if (MP <= 32) {
-    S = info.sm_count / ntiles;
-    if (S > kMaxCluster) S = kMaxCluster;
-    if (S > kblocks) S = kblocks;
-    if (S < 1) S = 1;
-  } else {
-    for (int cs = kMaxCluster < kblocks ? kMaxCluster : kblocks; cs > 1; --cs) {
-      int resident = 0;
-      if (int st = resident_clusters(cs, static_cast<int>(L::kAlloc), info, &resident)) return st;
-      if (ntiles <= resident) {
-        S = cs;
-        break;
-      }
+  for (int cs = kMaxCluster < kblocks ? kMaxCluster : kblocks; cs > 1; --cs) {
+    int resident = 0;
+    if (int st = resident_clusters(cs, static_cast<int>(L::kAlloc), info, &resident)) return st;
+    if (ntiles <= resident) {
+      S = cs;
+      break;
     }
   }
   const int kbps = (kblocks + S - 1) / S;
