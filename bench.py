@@ -186,6 +186,28 @@ class ClockSampler:
             self._thread.join(timeout=5)
         return False
 
+    def nvlink_kib(self):
+        """This GPU's NVLink data counters (TX, RX; KiB, summed over its
+        links) through NVML field values, or None where NVML does not
+        report them."""
+        if self._nvml is None:
+            return None
+        nv = self._nvml
+        try:
+            h = self._handle()
+            tx = rx = 0
+            for link in range(18):
+                vals = nv.nvmlDeviceGetFieldValues(h, [
+                    (nv.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_TX, link),
+                    (nv.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_RX, link)])
+                if vals[0].nvmlReturn or vals[1].nvmlReturn:
+                    continue
+                tx += int(vals[0].value.ullVal)
+                rx += int(vals[1].value.ullVal)
+            return tx, rx
+        except Exception:  # noqa: BLE001
+            return None
+
     def summary(self) -> dict:
         if self._nvml is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
@@ -313,6 +335,7 @@ def tp_timed(args, block, x, world: int, peaks: dict, guard) -> dict:
         evs = [(ev(), ev(), ev(), ev()) for _ in range(args.steps)]
         _meet(world)
         guard.check()
+        nv0 = clocks.nvlink_kib() if world > 1 else None
         t0, t1 = ev(), ev()
         t0.record()
         for a, b, c, d in evs:
@@ -321,6 +344,7 @@ def tp_timed(args, block, x, world: int, peaks: dict, guard) -> dict:
             d.record()
         t1.record()
         torch.cuda.synchronize()
+        nv1 = clocks.nvlink_kib() if nv0 is not None else None
     total_ms = t0.elapsed_time(t1)
     pre = statistics.mean(a.elapsed_time(b) for a, b, _, _ in evs)
     gu_ms = statistics.mean(b.elapsed_time(c) for _, b, c, _ in evs)
@@ -342,7 +366,26 @@ def tp_timed(args, block, x, world: int, peaks: dict, guard) -> dict:
                          "kernel": f"gemm_silu_mul + folded rms_norm, M={TOKENS} K={HIDDEN} "
                                    f"N={2 * INTER // world}"},
             "gpu_launches": block.launches_per_step() * args.steps,
-            "clocks": clocks.summary()}
+            "clocks": clocks.summary(),
+            "nvlink": nvlink_per_step(nv0, nv1, args.steps, world)}
+
+
+def nvlink_per_step(nv0, nv1, steps: int, world: int):
+    """NVLink data bytes per timed step per GPU (the largest over the ranks)
+    from the NVML counters read around the timed steps; every rank takes
+    part in the reduction, null where a rank had no counters."""
+    if world == 1:
+        return None
+    have = nv0 is not None and nv1 is not None
+    tx = (nv1[0] - nv0[0]) * 1024.0 / steps if have else -1.0
+    rx = (nv1[1] - nv0[1]) * 1024.0 / steps if have else -1.0
+    lo = _max_over_ranks([-tx, -rx], world)  # any rank without counters shows as +1
+    tx, rx = _max_over_ranks([tx, rx], world)
+    if lo[0] > 0 or lo[1] > 0 or tx <= 0:
+        return None
+    payload = 2.0 * TOKENS * HIDDEN
+    return {"tx_mb": round(tx / 1e6, 1), "rx_mb": round(rx / 1e6, 1),
+            "all_reduce_payload_mb": round(payload / 1e6, 1)}
 
 
 def tp_e2e(args, block, x, rank: int, world: int, guard) -> dict:
@@ -377,9 +420,8 @@ def tp_e2e(args, block, x, rank: int, world: int, guard) -> dict:
     return {"value": TOKENS / (ms * 1e-3), "unit": "tokens/s",
             "h2d_bytes_per_step": hs.h2d_bytes() * world, "d2h_bytes_per_step": hs.d2h_bytes() * world,
             "ms_per_step": round(ms, 4), "max_abs_diff_vs_device": diff,
-            "api": "aot_kernel.tp_mlp.HostStream.submit(x_host, out_host): each rank copies its "
-                   "1/N of the pinned input rows in, all-gather over NVLink, block, its 1/N of the "
-                   "output rows back; next batch's copy-in overlaps this batch's kernels"}
+            "api": "tp_mlp.HostStream.submit: 1/N of the pinned rows in per rank, all-gather, "
+                   "block, 1/N out"}
 
 
 def tp_parity(block, x, host: dict, rank: int) -> dict | None:
@@ -398,7 +440,7 @@ def tp_parity(block, x, host: dict, rank: int) -> dict | None:
     return {"rows": PARITY_ROWS, "max_abs_err": err, "max_abs_ref": scale,
             "err_frac": round(err / scale, 6), "tol_frac": PARITY_TOL,
             "pass": bool(err <= PARITY_TOL * scale),
-            "reference": "ref.rmsnorm -> ref.gemm -> ref.silu(gate) * up -> ref.gemm (torch CPU)"}
+            "reference": "ref ops on CPU"}
 
 
 # ---------------------------------------------------------------- the reference on the host
@@ -561,14 +603,20 @@ def kernel_table(peaks: dict) -> dict:
         outs = [torch.empty((M, N), device="cuda", dtype=torch.bfloat16) for _ in range(R)]
         calls = [lambda a=a, b=b, c=c: aot_kernel.gemm(a, b, out=c) for (a, b), c in zip(sets, outs)]
         ms = graph_launch_ms(calls)
-        del sets, outs, calls
+        # cuBLAS (torch.matmul) on the same operands: its time / ours
+        lib = [lambda a=a, b=b, c=c: torch.matmul(a, b, out=c) for (a, b), c in zip(sets, outs)]
+        try:
+            vs_lib = round(graph_launch_ms(lib) / ms, 3)
+        except Exception:  # noqa: BLE001  (library path unavailable on this build)
+            vs_lib = None
+        del sets, outs, calls, lib
         flops = 2.0 * M * N * K
         nbytes = 2.0 * (M * K + K * N + M * N)
         if flops / nbytes >= ridge:
             tf = flops / (ms * 1e-3) / 1e12
-            return [round(ms, 5), round(tf, 1), round(tf / peaks["bf16_tflops"], 3)]
+            return [round(ms, 5), round(tf, 1), round(tf / peaks["bf16_tflops"], 3), vs_lib]
         gbs = nbytes / (ms * 1e-3) / 1e9
-        return [round(ms, 5), round(gbs, 1), round(gbs / peaks["hbm_gbs"], 3)]
+        return [round(ms, 5), round(gbs, 1), round(gbs / peaks["hbm_gbs"], 3), vs_lib]
 
     for n in (2048, 4096, 8192, 16384):
         out[f"gemm_{n}^3"] = gemm_entry(n, n, n, 10 + n, n ** -0.5)
@@ -782,14 +830,14 @@ def run_ours(args, rank: int, world: int, local: int, guard, held: dict) -> dict
                            + ("down GEMM fused with an NVSwitch all-reduce" if world > 1 and
                               block.allreduce == "fused" else
                               "NCCL all-reduce" if world > 1 else "one GPU"))
-    line["phases_ms"] = head["phases_ms"]
-    line["tensor_frac_per_gpu"] = round(BLOCK_FLOPS / world / (peaks["bf16_tflops"] * 1e12)
-                                        / (head["ms_per_step"] * 1e-3), 4)
+    tensor_frac = round(BLOCK_FLOPS / world / (peaks["bf16_tflops"] * 1e12)
+                        / (head["ms_per_step"] * 1e-3), 4)
     if rank == 0 and world == 1 and not args.no_kernels:
         del block, held["block"]
         gc.collect()
         torch.cuda.empty_cache()
-        line["kernels_fields"] = "[ms, TFLOP/s or GB/s, fraction of the measured peak]"
+        line["kernels_fields"] = ("[ms, TFLOP/s or GB/s, fraction of the measured peak"
+                                  "(, 16-bit GEMMs: cuBLAS time / ours)]")
         line["kernels"] = kernel_table(peaks)
         line["gemm_8192"] = gemm_8192(args, peaks)
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -797,10 +845,38 @@ def run_ours(args, rank: int, world: int, local: int, guard, held: dict) -> dict
     wd = capi.watchdog_status(local)
     if wd:
         line["watchdog"] = wd
-    line.update({k: head[k] for k in ("gpu_launches", "clocks", "value", "ms_per_step", "roofline")})
+    line.update({k: head[k] for k in ("gpu_launches", "clocks", "roofline")})
     line["e2e"] = e2e
     line["tp_parity"] = parity
+    # Last, and short: the figures a reader of the line's tail needs.
+    line["phases_ms"] = head["phases_ms"]
+    line["tensor_frac_per_gpu"] = tensor_frac
+    if head["nvlink"] is not None:
+        line["nvlink_per_step_per_gpu"] = head["nvlink"]
+    if "kernels" in line:
+        line["glance"] = glance(line)
+    line.update({k: head[k] for k in ("value", "ms_per_step")})
     return line
+
+
+GLANCE = {"gemm_8192^3": "gemm_8192", "gemm_2048^3": "gemm_2048",
+          "lin_M1_K4096_N28672": "m1_n28672", "lin_M16_K4096_N28672": "m16_n28672",
+          "lin_M1_K4096_N6144": "m1_n6144", "lin_M128_K4096_N6144": "m128_n6144",
+          "lin_M1_K14336_N4096": "m1_down", "lin_M128_K14336_N4096": "m128_down",
+          "gate_up_silu_M8192_K4096_I14336": "gate_up_silu", "rms_norm_8192x4096": "rms_norm",
+          "rms_rstd_8192x4096": "rms_rstd", "add_rms_norm_8192x4096": "add_rms_norm",
+          "silu_8192x14336": "silu", "silu_mul_8192x14336": "silu_mul"}
+
+
+def glance(line: dict) -> dict:
+    """Roofline fraction (and cuBLAS time / ours where timed) of the kernels
+    a reader checks first."""
+    out = {}
+    for key, short in GLANCE.items():
+        e = line["kernels"].get(key)
+        if e:
+            out[short] = e[2] if len(e) < 4 or e[3] is None else [e[2], e[3]]
+    return out
 
 
 def main() -> None:
