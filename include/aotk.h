@@ -116,10 +116,11 @@ AOTK_API int aotk_rmsnorm_rstd(float* rstd, const void* x, int64_t rows, int64_t
 /* ---- gemm ------------------------------------------------------------- */
 
 /* Tensor-core GEMM for FLOAT16 / BFLOAT16 (FLOAT32 returns AOTK_ERR_UNSUPPORTED,
- * as the reference's gemm_opt rejects it).  Picks the persistent tcgen05
- * kernel, the skinny split-K tcgen05 kernel (M <= 128) or, for shapes TMA
- * cannot address (K or N not a multiple of 8, pointers not 16-byte aligned),
- * the SIMT kernel.
+ * as the reference's gemm_opt rejects it).  Picks the skinny split-K tcgen05
+ * kernel (M <= 128), the CTA-pair kernel on 256 x 512 tiles or the
+ * persistent 1-CTA tcgen05 kernel (whichever aotk_gemm_path names for the
+ * shape) or, for shapes TMA cannot address (K or N not a multiple of 8,
+ * pointers not 16-byte aligned), the SIMT kernel.
  * Replaces gemm_opt(Tensor! out, Tensor a, Tensor b)
  * (aot_kernel/csrc/gemm/gemm_opt.cu:165-195, registration.cc:23-24). */
 AOTK_API int aotk_gemm_opt(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
@@ -199,6 +200,25 @@ AOTK_API int aotk_gemm_tc(void* c, const void* a, const void* b, int64_t M, int6
  * B, one MMA of M = 256 reads both.  Same preconditions as aotk_gemm_tc. */
 AOTK_API int aotk_gemm_tc2(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
                            int dtype, void* stream);
+
+/* The CTA-pair kernel on 256 x 512 tiles: two MMAs of M = 256, N = 256 per K
+ * step into one 512-column accumulator per CTA (all of TMEM); each CTA stages
+ * 128 rows of A and 256 columns of B.  Half the operand bytes per flop of the
+ * 1-CTA kernel.  Same preconditions as aotk_gemm_tc. */
+AOTK_API int aotk_gemm_tc2w(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
+                            int dtype, void* stream);
+
+enum { AOTK_PATH_SIMT = 0, AOTK_PATH_SKINNY = 1, AOTK_PATH_TC = 2, AOTK_PATH_TC2_WIDE = 3 };
+
+/* The kernel aotk_gemm_opt_ws picks for a 16-bit problem on a device with
+ * `sm_count` SMs, given a workspace (with_workspace != 0) or not; assumes
+ * TMA-addressable operands (K % 8 == 0, N % 8 == 0, aligned pointers), else
+ * the path is AOTK_PATH_SIMT.  Pure host arithmetic: a cost model of whole
+ * rounds of tiles over the SMs (the 1-CTA kernel's cut last wave included)
+ * with the pair kernel's measured throughput advantage.  No reference
+ * counterpart (the reference has one tensor-core kernel). */
+AOTK_API int aotk_gemm_path(int64_t M, int64_t N, int64_t K, int sm_count, int with_workspace,
+                            int* path);
 
 /* Skinny (decode) kernel: computes C^T = B^T A^T on tcgen05 with the weight
  * streamed by TMA and K split across a thread-block cluster whose partial sums

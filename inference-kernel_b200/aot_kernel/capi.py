@@ -40,6 +40,8 @@ SIGNATURES: dict[str, list] = {
     "aotk_gemm": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
     "aotk_gemm_tc": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
     "aotk_gemm_tc2": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
+    "aotk_gemm_tc2w": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
+    "aotk_gemm_path": [_i64, _i64, _i64, _int, _int, ctypes.POINTER(ctypes.c_int)],
     "aotk_gemm_skinny": [_ptr, _ptr, _ptr, _i64, _i64, _i64, _int, _ptr],
     "aotk_watchdog_status": [_int, ctypes.POINTER(ctypes.c_uint32), _int],
     "aotk_gemm_allreduce_tiles": [_i64, _i64, ctypes.POINTER(ctypes.c_int64)],
@@ -208,6 +210,20 @@ def gemm_tc(c, a, b, M, N, K, dtype, stream=None) -> None:
 
 def gemm_tc2(c, a, b, M, N, K, dtype, stream=None) -> None:
     _gemm("aotk_gemm_tc2", c, a, b, M, N, K, dtype, stream)
+
+
+def gemm_tc2w(c, a, b, M, N, K, dtype, stream=None) -> None:
+    _gemm("aotk_gemm_tc2w", c, a, b, M, N, K, dtype, stream)
+
+
+PATHS = {0: "simt", 1: "skinny", 2: "tc", 3: "tc2_wide"}
+
+
+def gemm_path(M, N, K, sm_count, with_workspace=True) -> str:
+    """The kernel aotk_gemm_opt_ws picks for a 16-bit problem (host arithmetic)."""
+    p = ctypes.c_int(-1)
+    _call("aotk_gemm_path", M, N, K, sm_count, int(bool(with_workspace)), ctypes.byref(p))
+    return PATHS[p.value]
 
 
 def gemm_skinny(c, a, b, M, N, K, dtype, stream=None) -> None:

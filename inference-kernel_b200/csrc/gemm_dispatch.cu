@@ -4,7 +4,10 @@
 // workspace the persistent kernel also splits its partial last wave along K):
 //   16-bit, TMA-addressable, M <= 128  -> skinny swap-AB split-K kernel
 //                                          (decode; HBM-bound on the weight)
-//   16-bit, TMA-addressable, M > 128   -> persistent tcgen05 kernel
+//   16-bit, TMA-addressable, M > 128   -> the CTA-pair kernel on 256 x 512
+//                                          tiles or the persistent 1-CTA
+//                                          kernel on 128 x 256 tiles, by the
+//                                          cost model of gemm_opt_path
 //   anything else                       -> SIMT kernel
 // aotk_scaled_gemm (8-bit inputs): K % 16 == 0, N % 16 == 0, aligned -> the
 // persistent kernel on kind::f8f6f4 / kind::i8, else its SIMT kernel.
@@ -89,6 +92,34 @@ int check_tc_preconditions(const char* who, const void* c, const void* a, const 
   return AOTK_OK;
 }
 
+// Cost model behind aotk_gemm_opt's choice between the 1-CTA kernel
+// (128 x 256 tiles over all SMs, its partial last wave cut into N halves or K
+// splits by plan_tc) and the CTA-pair kernel (256 x 512 tiles over SM pairs).
+// Time is counted in rounds of 128 x 256 x K work per SM; a pair tile is two
+// such units per SM.  The pair kernel's throughput advantage on whole rounds
+// (kWideGain) is what was measured on B200 for K >= 4096 (8192^3 1.08-1.11x,
+// 8192 x 4096 x 28672 1.04-1.10x, 16384^3 1.06x); below K = 4096 its
+// unoverlapped epilogue weighs more and it is not chosen.  The cut last wave
+// of the 1-CTA kernel is charged more than its share of the work: N halves
+// 0.6 of a round, a 4-way K split 0.35 (measured tails run at lower
+// efficiency than whole tiles).  The pair kernel is chosen only when the
+// model gives it a 3 % margin.
+int gemm_opt_path(int64_t M, int64_t N, int64_t K, int sm_count, bool with_workspace) {
+  constexpr double kWideGain = 1.08;
+  constexpr double kMargin = 0.97;
+  if (M <= kSkinnyMaxM) return AOTK_PATH_SKINNY;
+  if (K < 4096 || sm_count < 2) return AOTK_PATH_TC;
+  int64_t sch[10];
+  if (gemm_tc_schedule(M, N, K, 2, sm_count, with_workspace, sch) != AOTK_OK) return AOTK_PATH_TC;
+  double tc = static_cast<double>(sch[2]);  // rounds of whole tiles
+  if (sch[4]) tc += 0.6;                    // last wave as N halves
+  else if (sch[5] > 1) tc += 0.35;          // last wave as K splits
+  const int64_t pair_tiles = ((M + 255) / 256) * ((N + 511) / 512);
+  const int64_t pairs = sm_count / 2;
+  const double wide = 2.0 * static_cast<double>((pair_tiles + pairs - 1) / pairs) / kWideGain;
+  return wide < kMargin * tc ? AOTK_PATH_TC2_WIDE : AOTK_PATH_TC;
+}
+
 }  // namespace aotk
 
 extern "C" int aotk_gemm_opt_ws(void* c, const void* a, const void* b, int64_t M, int64_t N,
@@ -102,6 +133,12 @@ extern "C" int aotk_gemm_opt_ws(void* c, const void* a, const void* b, int64_t M
   if (K == 0) return zero_output(c, M, N, dtype, stream);
   if (tc_eligible(c, a, b, M, N, K, dtype)) {
     if (M <= kSkinnyMaxM) return gemm_skinny(c, a, b, M, N, K, dtype, stream);
+    DeviceInfo info;
+    if (int st = current_device_info(&info)) return st;
+    const bool with_ws =
+        workspace != nullptr && workspace_bytes >= gemm_tc_workspace_size(M, N, K, info.sm_count);
+    if (gemm_opt_path(M, N, K, info.sm_count, with_ws) == AOTK_PATH_TC2_WIDE)
+      return gemm_tc2_wide(c, a, b, M, N, K, dtype, stream);
     return gemm_tc(c, a, b, M, N, K, dtype, workspace, workspace_bytes, stream);
   }
   return gemm_simt(c, a, b, M, N, K, dtype, stream);
@@ -123,6 +160,9 @@ extern "C" int aotk_gemm_opt_workspace_size(int64_t M, int64_t N, int64_t K, int
   if (M <= kSkinnyMaxM || K % 8 != 0 || N % 8 != 0) return AOTK_OK;
   DeviceInfo info;
   if (int st = current_device_info(&info)) return st;
+  // The pair kernel needs no scratch; it is chosen without a workspace
+  // whenever it is chosen with one (the 1-CTA kernel only gets slower).
+  if (gemm_opt_path(M, N, K, info.sm_count, true) == AOTK_PATH_TC2_WIDE) return AOTK_OK;
   *bytes = gemm_tc_workspace_size(M, N, K, info.sm_count);
   return AOTK_OK;
 }
@@ -143,6 +183,24 @@ extern "C" int aotk_gemm_tc(void* c, const void* a, const void* b, int64_t M, in
 extern "C" int aotk_gemm_tc2(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
                              int dtype, void* stream) {
   return aotk::gemm_tc2(c, a, b, M, N, K, dtype, stream);
+}
+
+extern "C" int aotk_gemm_tc2w(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
+                              int dtype, void* stream) {
+  return aotk::gemm_tc2_wide(c, a, b, M, N, K, dtype, stream);
+}
+
+extern "C" int aotk_gemm_path(int64_t M, int64_t N, int64_t K, int sm_count, int with_workspace,
+                              int* path) {
+  using namespace aotk;
+  if (!path || M <= 0 || N <= 0 || K <= 0 || sm_count <= 0)
+    return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_gemm_path: bad arguments");
+  if (K % 8 != 0 || N % 8 != 0 || M >= (1LL << 31) || N >= (1LL << 31) || K >= (1LL << 31)) {
+    *path = AOTK_PATH_SIMT;
+    return AOTK_OK;
+  }
+  *path = gemm_opt_path(M, N, K, sm_count, with_workspace != 0);
+  return AOTK_OK;
 }
 
 extern "C" int aotk_gemm_skinny(void* c, const void* a, const void* b, int64_t M, int64_t N,

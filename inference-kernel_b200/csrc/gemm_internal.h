@@ -47,6 +47,14 @@ int gemm_scaled_simt(void* c, const void* a, const void* b, const float* scale_a
 // Persistent tcgen05 GEMM on CTA pairs, 256 x 256 tiles (gemm_tc2.cu).
 int gemm_tc2(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K, int dtype,
              void* stream);
+// The same on 256 x 512 tiles (one 512-column accumulator per CTA).
+int gemm_tc2_wide(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
+                  int dtype, void* stream);
+
+// Which kernel aotk_gemm_opt runs for a TMA-eligible 16-bit problem on
+// `sm_count` SMs (pure host arithmetic): AOTK_PATH_SKINNY, AOTK_PATH_TC or
+// AOTK_PATH_TC2_WIDE (gemm_dispatch.cu).
+int gemm_opt_path(int64_t M, int64_t N, int64_t K, int sm_count, bool with_workspace);
 int tc2_watchdog(uint32_t* status, bool clear);
 
 // Persistent tcgen05 GEMM fused with an all-reduce of C over NVSwitch

@@ -1,19 +1,28 @@
 // Persistent tcgen05 GEMM on CTA pairs: C[M,N] = A[M,K] * B[K,N].
 //
-// A cluster of two CTAs (on two SMs) computes 256 x 256 output tiles with one
-// tcgen05.mma.cta_group::2 per K step (M = 256, N = 256, K = 16):
-//   * CTA r of the pair TMA-loads rows [m0 + 128r, +128) of A and columns
-//     [n0 + 128r, +128) of B into its own shared memory (4-6 stage ring); the
-//     MMA reads both CTAs' halves, so each SM stages half the B traffic of a
-//     128 x 256 tile for twice the math.  No load is multicast.
+// A cluster of two CTAs (on two SMs) computes 256 x BNP output tiles with
+// tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16), BNP = 256 (one MMA per
+// K step) or 512 (two, into a 512-column accumulator that fills TMEM):
+//   * CTA r of the pair TMA-loads rows [m0 + 128r, +128) of A and, for each
+//     256-column MMA h, columns [n0 + 256h + 128r, +128) of B into its own
+//     shared memory; the MMA reads both CTAs' halves.  Per 64-deep K block an
+//     SM stages 32 KB for 128 x 256 x 64 of MMA work (BNP = 256) or 48 KB for
+//     128 x 512 x 64 (BNP = 512) - against 48 KB for 128 x 256 x 64 in the
+//     1-CTA kernel - so the wide tile moves half as many operand bytes per
+//     flop through L2 and shared memory, and its 4-stage ring covers twice
+//     the MMA time.  On B200, where these GEMMs run at the 1 kW power cap,
+//     fewer bytes moved per flop show up as clock and tensor-pipe occupancy
+//     (8192^3: 1.08-1.11x the 1-CTA kernel).  No load is multicast.
 //   * The full barrier of a stage lives in the first CTA: its producer
 //     expects the bytes of both CTAs' loads, the second CTA's loads complete
 //     their bytes there.  The first CTA's MMA warp issues all MMAs and its
 //     commits arrive on the empty / accumulator-full barriers of both CTAs.
 //   * Each CTA's four epilogue warps read their 128 accumulator rows from
-//     their own TMEM (two 256-column accumulators, so the epilogue of one tile
-//     overlaps the MMAs of the next), release the accumulator on the first
-//     CTA's barrier and TMA-store 32 x 64 boxes of C.
+//     their own TMEM (BNP = 256: two 256-column accumulators, so the epilogue
+//     of one tile overlaps the MMAs of the next; BNP = 512: one, so the next
+//     tile's MMAs wait for its read-out; splitting the read-out over eight
+//     warps measured no faster), release the accumulator on the first CTA's
+//     barrier and TMA-store 32 x 64 boxes of C.
 // Every wait is bounded (sm100.cuh); both CTAs meet at a cluster barrier
 // before TMEM is freed and before either exits.
 #include <type_traits>
@@ -32,21 +41,28 @@ using namespace sm100;
 __device__ unsigned g_tc2_watchdog;
 
 constexpr int kBM = 256;      // rows per pair tile (128 per CTA)
-constexpr int kBN = 256;      // columns per pair tile (128 of B per CTA)
 constexpr int kHalf = 128;
 constexpr int kBK = 64;
 constexpr int kUmmaK = 16;
-constexpr int kThreads = 192;
+constexpr int kThreads = 192;  // producer, MMA and 4 epilogue warps
 constexpr int kGroupM = 8;    // M pair-tiles per raster group
-constexpr uint32_t kTmemCols = 2 * kBN;
+constexpr uint32_t kTmemCols = 512;  // all of TMEM: 2 x 256 or 1 x 512 accumulator columns
 
 enum : unsigned { kWdProducer = 256u, kWdMma = 512u, kWdEpilogue = 1024u };
 
-template <int STAGES>
+// BNP = columns per pair tile: 256 (one MMA of N = 256 per K step, two
+// accumulators so the epilogue of one tile overlaps the next tile's MMAs) or
+// 512 (two MMAs of N = 256 per K step into one 512-column accumulator, which
+// fills TMEM: each SM then stages 48 KB of operands per 128 x 512 x 64 of
+// MMA work instead of 32 KB per 128 x 256 x 64).
+template <int STAGES, int BNP>
 struct Tc2Layout {
+  static constexpr int kMmas = BNP / 256;               // MMAs of N = 256 per K step
+  static constexpr int kAccs = BNP == 256 ? 2 : 1;      // accumulators in TMEM
   static constexpr uint32_t kABytes = kHalf * kBK * 2;  // this CTA's 128 rows of A
   static constexpr uint32_t kBBox = kBK * 128;          // 64 (N) x 64 (K)
-  static constexpr uint32_t kBBytes = 2 * kBBox;        // this CTA's 128 columns of B
+  static constexpr int kBBoxes = BNP / 2 / 64;          // this CTA's BNP / 2 columns of B
+  static constexpr uint32_t kBBytes = kBBoxes * kBBox;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr uint32_t kPairStageBytes = 2 * kStageBytes;
   static constexpr uint32_t kCBuf = 32 * 128;
@@ -58,6 +74,8 @@ struct Tc2Layout {
   static constexpr uint32_t kOffMisc = kOffBar + kNumBars * 8;
   static constexpr uint32_t kBytes = kOffMisc + 16;
   static constexpr uint32_t kAlloc = kBytes + 1024;
+  static_assert(BNP == 256 || BNP == 512, "pair tiles are 256 or 512 columns wide");
+  static_assert(kAccs * BNP <= static_cast<int>(kTmemCols), "accumulators must fit in TMEM");
 };
 
 __device__ __forceinline__ void pair_tile_coords(int tile, int tiles_m, int tiles_n, int& mb,
@@ -71,11 +89,12 @@ __device__ __forceinline__ void pair_tile_coords(int tile, int tiles_m, int tile
   nb = local / gm;
 }
 
-template <typename T, int STAGES>
+template <typename T, int STAGES, int BNP>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmC, int M, int N, int K, uint32_t idesc) {
-  using L = Tc2Layout<STAGES>;
+  using L = Tc2Layout<STAGES, BNP>;
+  constexpr int kBN = BNP;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -140,7 +159,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         int mb, nb;
         pair_tile_coords(tile, tiles_m, tiles_n, mb, nb);
         const int row0 = mb * kBM + static_cast<int>(rank) * kHalf;
-        const int col0 = nb * kBN + static_cast<int>(rank) * kHalf;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, wd, kWdProducer)) {
             ok = false;
@@ -150,8 +168,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t fb = map_to_rank(full_bar(stage), 0);
           if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), L::kPairStageBytes);
           tma_load_2d_pair(sA + stage * L::kABytes, &tmA, kb * kBK, row0, fb);
-          tma_load_2d_pair(sB + stage * L::kBBytes, &tmB, col0, kb * kBK, fb);
-          tma_load_2d_pair(sB + stage * L::kBBytes + L::kBBox, &tmB, col0 + 64, kb * kBK, fb);
+          // Box j feeds MMA j / 2 (columns [256 h, 256 h + 256) of the tile),
+          // of which this CTA stages the half [128 rank, 128 rank + 128).
+#pragma unroll
+          for (int j = 0; j < L::kBBoxes; ++j)
+            tma_load_2d_pair(sB + stage * L::kBBytes + j * L::kBBox, &tmB,
+                             nb * kBN + (j / 2) * 256 + static_cast<int>(rank) * kHalf + (j % 2) * 64,
+                             kb * kBK, fb);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -199,8 +222,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < kBK / kUmmaK; ++k) {
             const uint64_t ad = sdesc_sw128(a0 + k * kUmmaK * 2, 16, 1024);
-            const uint64_t bd = sdesc_sw128(b0 + k * kUmmaK * 128, L::kBBox, 1024);
-            umma_f16_pair(d_tmem, ad, bd, idesc, kb > 0 || k > 0);
+#pragma unroll
+            for (int h = 0; h < L::kMmas; ++h) {
+              const uint64_t bd =
+                  sdesc_sw128(b0 + h * 2 * L::kBBox + k * kUmmaK * 128, L::kBBox, 1024);
+              umma_f16_pair(d_tmem + h * 256, ad, bd, idesc, kb > 0 || k > 0);
+            }
           }
           umma_commit_pair(empty_bar(stage), 0x3);
           if (++stage == STAGES) {
@@ -210,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         umma_commit_pair(tfull_bar(acc), 0x3);
-        if (++acc == 2) {
+        if (++acc == L::kAccs) {
           acc = 0;
           acc_phase ^= 1u;
         }
@@ -271,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ++nstore;
       }
-      if (++acc == 2) {
+      if (++acc == L::kAccs) {
         acc = 0;
         acc_phase ^= 1u;
       }
@@ -291,11 +318,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <typename T, int STAGES>
+template <typename T, int STAGES, int BNP>
 int launch_tc2(void* c, const void* a, const void* b, int M, int N, int K, bool bf16,
                cudaStream_t stream, const DeviceInfo& info) {
-  using L = Tc2Layout<STAGES>;
-  auto kernel = gemm_tc2_kernel<T, STAGES>;
+  using L = Tc2Layout<STAGES, BNP>;
+  constexpr int kBN = BNP;
+  auto kernel = gemm_tc2_kernel<T, STAGES, BNP>;
   if (int st = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), L::kAlloc, info)) return st;
   CUtensorMap ta, tb, tc;
   if (int st = make_tmap_2d_16bit(&ta, a, bf16, M, K, K, kBK, kHalf)) return st;
@@ -316,14 +344,16 @@ int launch_tc2(void* c, const void* a, const void* b, int M, int N, int K, bool 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const uint32_t idesc = idesc_f16(bf16, kBM, kBN, /*a_mn_major=*/false, /*b_mn_major=*/true);
+  // Every MMA is M = 256 (128 rows per CTA) x N = 256.
+  const uint32_t idesc = idesc_f16(bf16, kBM, 256, /*a_mn_major=*/false, /*b_mn_major=*/true);
   cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, M, N, K, idesc);
   if (e != cudaSuccess)
     return fail(AOTK_ERR_CUDA, "tcgen05 pair gemm launch: %s", cudaGetErrorString(e));
   return check_launch("tcgen05 pair gemm");
 }
 
-constexpr int kTc2Stages = 6;
+constexpr int kTc2Stages = 6;      // 256-column pair tiles: 6 x 32 KB stages
+constexpr int kTc2WideStages = 4;  // 512-column pair tiles: 4 x 48 KB stages
 
 }  // namespace
 
@@ -336,8 +366,21 @@ int gemm_tc2(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int m = (int)M, n = (int)N, k = (int)K;
   if (dtype == AOTK_BFLOAT16)
-    return launch_tc2<__nv_bfloat16, kTc2Stages>(c, a, b, m, n, k, true, s, info);
-  return launch_tc2<__half, kTc2Stages>(c, a, b, m, n, k, false, s, info);
+    return launch_tc2<__nv_bfloat16, kTc2Stages, 256>(c, a, b, m, n, k, true, s, info);
+  return launch_tc2<__half, kTc2Stages, 256>(c, a, b, m, n, k, false, s, info);
+}
+
+int gemm_tc2_wide(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
+                  int dtype, void* stream) {
+  DeviceInfo info;
+  if (int st = current_device_info(&info)) return st;
+  if (int st = require_sm100(info)) return st;
+  if (int st = check_tc_preconditions("aotk_gemm_tc2w", c, a, b, M, N, K, dtype)) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int m = (int)M, n = (int)N, k = (int)K;
+  if (dtype == AOTK_BFLOAT16)
+    return launch_tc2<__nv_bfloat16, kTc2WideStages, 512>(c, a, b, m, n, k, true, s, info);
+  return launch_tc2<__half, kTc2WideStages, 512>(c, a, b, m, n, k, false, s, info);
 }
 
 int tc2_watchdog(uint32_t* status, bool clear) {

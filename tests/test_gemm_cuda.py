@@ -118,6 +118,24 @@ def test_capi_gemm_tc2(shape, dt):
     assert capi.watchdog_status() == 0
 
 
+# The 256 x 512 pair tile: partial tiles in M (rows of the second CTA past M)
+# and N (the second MMA's columns past N), a single tile, several waves.
+TC2W_SHAPES = TC_SHAPES + [(256, 64, 512), (520, 4096, 1544), (8192, 1024, 2048),
+                           (2304, 512, 5120)]
+
+
+@pytest.mark.parametrize("shape", TC2W_SHAPES, ids=str)
+@pytest.mark.parametrize("dt", ["bfloat16", "float16"])
+def test_capi_gemm_tc2w(shape, dt):
+    from aot_kernel import capi
+
+    M, K, N = shape
+    a, b = _inputs(M, K, N, dt, seed=5 * M + N)
+    got = _run_capi(capi.gemm_tc2w, a, b, dt)
+    assert_close_for_gemm(got, ops.gemm(a, b, dt), dt)
+    assert capi.watchdog_status() == 0
+
+
 SKINNY = [(1, 64, 256), (1, 4096, 1024), (3, 328, 520), (16, 1024, 2048), (17, 512, 264),
           (64, 2048, 768), (100, 1000, 1032), (128, 4096, 512)]
 
@@ -180,6 +198,8 @@ FULL = [
     (128, 14336, 4096),
     (2048, 4096, 28672),
     (8192, 14336, 4096),
+    (8192, 4096, 28672),      # the pair kernel on 256 x 512 tiles (aotk_gemm_path)
+    (2048, 14336, 4096),
 ]
 
 

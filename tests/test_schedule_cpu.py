@@ -106,3 +106,33 @@ def test_schedule_rejects_bad_arguments():
         capi.gemm_schedule(0, 16, 16, 2, SMS, False)
     with pytest.raises(capi.AotkError):
         capi.gemm_schedule(16, 16, 16, 4, SMS, False)
+
+
+# ---- aotk_gemm_opt's kernel choice (aotk_gemm_path) ----
+
+@pytest.mark.parametrize("shape,path", [
+    ((1, 4096, 28672), "skinny"), ((128, 14336, 4096), "skinny"),
+    ((8192, 8192, 8192), "tc2_wide"), ((16384, 16384, 16384), "tc2_wide"),
+    ((8192, 4096, 28672), "tc2_wide"), ((4096, 8192, 57344), "tc2_wide"),
+    ((4096, 28672, 8192), "tc"),      # 256 pair tiles: 3.5 rounds on 74 pairs
+    ((4096, 4096, 4096), "tc"), ((2048, 2048, 2048), "tc"), ((8192, 2048, 8192), "tc"),
+    ((8192, 4100, 8192), "simt"), ((8192, 8192, 8190), "simt")], ids=str)
+def test_gemm_path_choices(shape, path):
+    M, K, N = shape
+    assert capi.gemm_path(M, N, K, SMS) == path
+
+
+def test_gemm_path_without_workspace_keeps_the_pair_kernel():
+    """The pair kernel needs no scratch: where it is chosen with a workspace
+    it is chosen without one too (only the 1-CTA kernel's tail gets slower),
+    so aotk_gemm_opt_workspace_size may report 0 for those shapes."""
+    for M, K, N in itertools.product((256, 1000, 2048, 4096, 8192), (4096, 8192, 14336),
+                                     (1024, 4096, 6144, 14336, 28672)):
+        if capi.gemm_path(M, N, K, SMS, True) == "tc2_wide":
+            assert capi.gemm_path(M, N, K, SMS, False) == "tc2_wide", (M, K, N)
+
+
+def test_gemm_path_rejects_bad_arguments():
+    with pytest.raises(capi.AotkError):
+        capi.gemm_path(0, 8, 8, SMS)
+
