@@ -117,7 +117,7 @@ AOTK_API int aotk_rmsnorm_rstd(float* rstd, const void* x, int64_t rows, int64_t
 
 /* Tensor-core GEMM for FLOAT16 / BFLOAT16 (FLOAT32 returns AOTK_ERR_UNSUPPORTED,
  * as the reference's gemm_opt rejects it).  Picks the skinny split-K tcgen05
- * kernel (M <= 128), the CTA-pair kernel on 256 x 512 tiles or the
+ * kernel (M <= 128), a CTA-pair kernel (256 x 512 or 256 x 256 tiles) or the
  * persistent 1-CTA tcgen05 kernel (whichever aotk_gemm_path names for the
  * shape) or, for shapes TMA cannot address (K or N not a multiple of 8,
  * pointers not 16-byte aligned), the SIMT kernel.
@@ -208,7 +208,13 @@ AOTK_API int aotk_gemm_tc2(void* c, const void* a, const void* b, int64_t M, int
 AOTK_API int aotk_gemm_tc2w(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
                             int dtype, void* stream);
 
-enum { AOTK_PATH_SIMT = 0, AOTK_PATH_SKINNY = 1, AOTK_PATH_TC = 2, AOTK_PATH_TC2_WIDE = 3 };
+enum {
+  AOTK_PATH_SIMT = 0,      /* aotk_gemm's SIMT kernel */
+  AOTK_PATH_SKINNY = 1,    /* aotk_gemm_skinny */
+  AOTK_PATH_TC = 2,        /* aotk_gemm_tc */
+  AOTK_PATH_TC2_WIDE = 3,  /* aotk_gemm_tc2w */
+  AOTK_PATH_TC2 = 4        /* aotk_gemm_tc2 */
+};
 
 /* The kernel aotk_gemm_opt_ws picks for a 16-bit problem on a device with
  * `sm_count` SMs, given a workspace (with_workspace != 0) or not; assumes
@@ -236,10 +242,13 @@ AOTK_API int aotk_gemm_skinny(void* c, const void* a, const void* b, int64_t M, 
  * with W_gate and W_up interleaved in blocks of 128 columns:
  * columns [256j, 256j + 128) = W_gate[:, 128j : 128j + 128], columns
  * [256j + 128, 256j + 256) = W_up[:, 128j : 128j + 128]; I % 128 == 0,
- * K % 8 == 0, FLOAT16/BFLOAT16, 16-byte aligned pointers.  M > 128 runs on
- * the persistent tcgen05 kernel; a workspace of
- * aotk_gemm_silu_mul_workspace_size bytes enables the K-split last wave as
- * in aotk_gemm_opt_ws.  No reference counterpart (the reference composes
+ * K % 8 == 0, FLOAT16/BFLOAT16, 16-byte aligned pointers.  Runs on the
+ * kernel aotk_gemm_path names for the [M, K] x [K, 2I] product - a
+ * CTA-pair kernel (a 256 x 512 tile holds two gate/up block pairs, a 256 x
+ * 256 one) or the persistent 1-CTA kernel (also for M <= 128); for the
+ * latter a workspace of aotk_gemm_silu_mul_workspace_size bytes (0 when a
+ * pair kernel is chosen) enables the K-split last wave as in
+ * aotk_gemm_opt_ws.  No reference counterpart (the reference composes
  * ref.silu(a @ W_gate) * (a @ W_up)). */
 AOTK_API int aotk_gemm_silu_mul(void* act, const void* a, const void* b_gate_up, int64_t M,
                                 int64_t I, int64_t K, int dtype, void* workspace,

@@ -216,7 +216,7 @@ def gemm_tc2w(c, a, b, M, N, K, dtype, stream=None) -> None:
     _gemm("aotk_gemm_tc2w", c, a, b, M, N, K, dtype, stream)
 
 
-PATHS = {0: "simt", 1: "skinny", 2: "tc", 3: "tc2_wide"}
+PATHS = {0: "simt", 1: "skinny", 2: "tc", 3: "tc2_wide", 4: "tc2"}
 
 
 def gemm_path(M, N, K, sm_count, with_workspace=True) -> str:

@@ -5,9 +5,10 @@
 //   16-bit, TMA-addressable, M <= 128  -> skinny swap-AB split-K kernel
 //                                          (decode; HBM-bound on the weight)
 //   16-bit, TMA-addressable, M > 128   -> the CTA-pair kernel on 256 x 512
-//                                          tiles or the persistent 1-CTA
-//                                          kernel on 128 x 256 tiles, by the
-//                                          cost model of gemm_opt_path
+//                                          or 256 x 256 tiles or the
+//                                          persistent 1-CTA kernel on 128 x
+//                                          256 tiles, by the cost model of
+//                                          gemm_opt_path
 //   anything else                       -> SIMT kernel
 // aotk_scaled_gemm (8-bit inputs): K % 16 == 0, N % 16 == 0, aligned -> the
 // persistent kernel on kind::f8f6f4 / kind::i8, else its SIMT kernel.
@@ -92,21 +93,25 @@ int check_tc_preconditions(const char* who, const void* c, const void* a, const 
   return AOTK_OK;
 }
 
-// Cost model behind aotk_gemm_opt's choice between the 1-CTA kernel
-// (128 x 256 tiles over all SMs, its partial last wave cut into N halves or K
-// splits by plan_tc) and the CTA-pair kernel (256 x 512 tiles over SM pairs).
-// Time is counted in rounds of 128 x 256 x K work per SM; a pair tile is two
-// such units per SM.  The pair kernel's throughput advantage on whole rounds
-// (kWideGain) is what was measured on B200 for K >= 4096 (8192^3 1.08-1.11x,
-// 8192 x 4096 x 28672 1.04-1.10x, 16384^3 1.06x); below K = 4096 its
-// unoverlapped epilogue weighs more and it is not chosen.  The cut last wave
-// of the 1-CTA kernel is charged more than its share of the work: N halves
-// 0.6 of a round, a 4-way K split 0.35 (measured tails run at lower
-// efficiency than whole tiles).  The pair kernel is chosen only when the
-// model gives it a 3 % margin.
+// Cost model behind aotk_gemm_opt's choice among the 1-CTA kernel (128 x 256
+// tiles over all SMs, its partial last wave cut into N halves or K splits by
+// plan_tc) and the CTA-pair kernel on 256 x 256 or 256 x 512 tiles (over SM
+// pairs).  Time is counted in rounds of 128 x 256 x K work per SM; a 256 x 256
+// pair tile is one such unit per SM, a 256 x 512 one two.  The pair kernels'
+// throughput advantage on whole rounds is what was measured on B200 with each
+// kernel running back to back for 0.6 s at the 1 kW power cap (as GEMMs run
+// inside a model step): 256 x 256 1.04-1.08x, 256 x 512 1.07-1.10x the 1-CTA
+// kernel (8192^3, 4096 x 8192 x 57344, 8192 x 4096 x 28672, 4096 x 28672 x
+// 8192).  Below K = 4096 the pair kernels are not chosen (untimed there; the
+// 256 x 512 tile's epilogue is not overlapped with the next tile).  The cut
+// last wave of the 1-CTA kernel is charged more than its share of the work
+// (N halves 0.6 of a round, a 4-way K split 0.35: tails run at lower
+// efficiency than whole tiles).  A pair kernel is chosen when it beats the
+// 1-CTA kernel's cost by 2 %.
 int gemm_opt_path(int64_t M, int64_t N, int64_t K, int sm_count, bool with_workspace) {
-  constexpr double kWideGain = 1.08;
-  constexpr double kMargin = 0.97;
+  constexpr double kPairGain = 1.05;
+  constexpr double kWideGain = 1.09;
+  constexpr double kMargin = 0.98;
   if (M <= kSkinnyMaxM) return AOTK_PATH_SKINNY;
   if (K < 4096 || sm_count < 2) return AOTK_PATH_TC;
   int64_t sch[10];
@@ -114,10 +119,13 @@ int gemm_opt_path(int64_t M, int64_t N, int64_t K, int sm_count, bool with_works
   double tc = static_cast<double>(sch[2]);  // rounds of whole tiles
   if (sch[4]) tc += 0.6;                    // last wave as N halves
   else if (sch[5] > 1) tc += 0.35;          // last wave as K splits
-  const int64_t pair_tiles = ((M + 255) / 256) * ((N + 511) / 512);
   const int64_t pairs = sm_count / 2;
-  const double wide = 2.0 * static_cast<double>((pair_tiles + pairs - 1) / pairs) / kWideGain;
-  return wide < kMargin * tc ? AOTK_PATH_TC2_WIDE : AOTK_PATH_TC;
+  auto rounds = [&](int64_t tiles) { return static_cast<double>((tiles + pairs - 1) / pairs); };
+  const double pair = rounds(((M + 255) / 256) * ((N + 255) / 256)) / kPairGain;
+  const double wide = 2.0 * rounds(((M + 255) / 256) * ((N + 511) / 512)) / kWideGain;
+  if (wide <= pair && wide < kMargin * tc) return AOTK_PATH_TC2_WIDE;
+  if (pair < wide && pair < kMargin * tc) return AOTK_PATH_TC2;
+  return AOTK_PATH_TC;
 }
 
 }  // namespace aotk
@@ -137,9 +145,14 @@ extern "C" int aotk_gemm_opt_ws(void* c, const void* a, const void* b, int64_t M
     if (int st = current_device_info(&info)) return st;
     const bool with_ws =
         workspace != nullptr && workspace_bytes >= gemm_tc_workspace_size(M, N, K, info.sm_count);
-    if (gemm_opt_path(M, N, K, info.sm_count, with_ws) == AOTK_PATH_TC2_WIDE)
-      return gemm_tc2_wide(c, a, b, M, N, K, dtype, stream);
-    return gemm_tc(c, a, b, M, N, K, dtype, workspace, workspace_bytes, stream);
+    switch (gemm_opt_path(M, N, K, info.sm_count, with_ws)) {
+      case AOTK_PATH_TC2_WIDE:
+        return gemm_tc2_wide(c, a, b, M, N, K, dtype, stream);
+      case AOTK_PATH_TC2:
+        return gemm_tc2(c, a, b, M, N, K, dtype, stream);
+      default:
+        return gemm_tc(c, a, b, M, N, K, dtype, workspace, workspace_bytes, stream);
+    }
   }
   return gemm_simt(c, a, b, M, N, K, dtype, stream);
 }
@@ -160,9 +173,9 @@ extern "C" int aotk_gemm_opt_workspace_size(int64_t M, int64_t N, int64_t K, int
   if (M <= kSkinnyMaxM || K % 8 != 0 || N % 8 != 0) return AOTK_OK;
   DeviceInfo info;
   if (int st = current_device_info(&info)) return st;
-  // The pair kernel needs no scratch; it is chosen without a workspace
+  // The pair kernels need no scratch; one is chosen without a workspace
   // whenever it is chosen with one (the 1-CTA kernel only gets slower).
-  if (gemm_opt_path(M, N, K, info.sm_count, true) == AOTK_PATH_TC2_WIDE) return AOTK_OK;
+  if (gemm_opt_path(M, N, K, info.sm_count, true) != AOTK_PATH_TC) return AOTK_OK;
   *bytes = gemm_tc_workspace_size(M, N, K, info.sm_count);
   return AOTK_OK;
 }
@@ -218,9 +231,36 @@ extern "C" int aotk_gemm_silu_mul_workspace_size(int64_t M, int64_t I, int64_t K
   if (dtype != AOTK_FLOAT16 && dtype != AOTK_BFLOAT16) return AOTK_OK;
   DeviceInfo info;
   if (int st = current_device_info(&info)) return st;
+  if (M > kSkinnyMaxM && gemm_opt_path(M, 2 * I, K, info.sm_count, true) != AOTK_PATH_TC)
+    return AOTK_OK;
   *bytes = gemm_tc_workspace_size(M, 2 * I, K, info.sm_count);
   return AOTK_OK;
 }
+
+namespace aotk {
+namespace {
+
+// gemm_silu_mul on the kernel aotk_gemm_path names for the [K, 2I] product:
+// a CTA-pair kernel or the persistent 1-CTA kernel (also for M <= 128, which
+// has no skinny silu_mul variant).
+int silu_mul_dispatch(void* act, const void* a, const void* b, const float* row_scale, int64_t M,
+                      int64_t N2, int64_t K, int dtype, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  if (tc_eligible(act, a, b, M, N2, K, dtype) && N2 % 256 == 0 && M > kSkinnyMaxM) {
+    DeviceInfo info;
+    if (int st = current_device_info(&info)) return st;
+    const bool with_ws = workspace != nullptr &&
+                         workspace_bytes >= gemm_tc_workspace_size(M, N2, K, info.sm_count);
+    const int path = gemm_opt_path(M, N2, K, info.sm_count, with_ws);
+    if (path == AOTK_PATH_TC2_WIDE || path == AOTK_PATH_TC2)
+      return gemm_tc2_silu_mul(act, a, b, row_scale, M, N2, K, dtype, path == AOTK_PATH_TC2_WIDE,
+                               stream);
+  }
+  return gemm_silu_mul(act, a, b, row_scale, M, N2, K, dtype, workspace, workspace_bytes, stream);
+}
+
+}  // namespace
+}  // namespace aotk
 
 extern "C" int aotk_gemm_silu_mul(void* act, const void* a, const void* b_gate_up, int64_t M,
                                   int64_t I, int64_t K, int dtype, void* workspace,
@@ -228,8 +268,8 @@ extern "C" int aotk_gemm_silu_mul(void* act, const void* a, const void* b_gate_u
   using namespace aotk;
   if (I < 0) return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_gemm_silu_mul: negative size");
   if (M == 0 || I == 0) return AOTK_OK;
-  return gemm_silu_mul(act, a, b_gate_up, nullptr, M, 2 * I, K, dtype, workspace, workspace_bytes,
-                       stream);
+  return silu_mul_dispatch(act, a, b_gate_up, nullptr, M, 2 * I, K, dtype, workspace,
+                           workspace_bytes, stream);
 }
 
 extern "C" int aotk_gemm_silu_mul_rowscale(void* act, const void* a, const void* b_gate_up,
@@ -241,8 +281,8 @@ extern "C" int aotk_gemm_silu_mul_rowscale(void* act, const void* a, const void*
   if (M == 0 || I == 0) return AOTK_OK;
   if (!row_scale)
     return fail(AOTK_ERR_INVALID_ARGUMENT, "aotk_gemm_silu_mul_rowscale: null row_scale");
-  return gemm_silu_mul(act, a, b_gate_up, row_scale, M, 2 * I, K, dtype, workspace,
-                       workspace_bytes, stream);
+  return silu_mul_dispatch(act, a, b_gate_up, row_scale, M, 2 * I, K, dtype, workspace,
+                           workspace_bytes, stream);
 }
 
 namespace aotk {

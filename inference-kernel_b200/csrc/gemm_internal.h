@@ -50,10 +50,15 @@ int gemm_tc2(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_
 // The same on 256 x 512 tiles (one 512-column accumulator per CTA).
 int gemm_tc2_wide(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
                   int dtype, void* stream);
+// A pair kernel (256 x 512 tiles when `wide`, else 256 x 256) with
+// gemm_silu_mul's epilogue (interleaved [K, N2] weight, act [M, N2 / 2],
+// optional fp32 row scale).
+int gemm_tc2_silu_mul(void* act, const void* a, const void* b, const float* row_scale, int64_t M,
+                      int64_t N2, int64_t K, int dtype, bool wide, void* stream);
 
 // Which kernel aotk_gemm_opt runs for a TMA-eligible 16-bit problem on
-// `sm_count` SMs (pure host arithmetic): AOTK_PATH_SKINNY, AOTK_PATH_TC or
-// AOTK_PATH_TC2_WIDE (gemm_dispatch.cu).
+// `sm_count` SMs (pure host arithmetic): AOTK_PATH_SKINNY, AOTK_PATH_TC,
+// AOTK_PATH_TC2 or AOTK_PATH_TC2_WIDE (gemm_dispatch.cu).
 int gemm_opt_path(int64_t M, int64_t N, int64_t K, int sm_count, bool with_workspace);
 int tc2_watchdog(uint32_t* status, bool clear);
 

@@ -89,12 +89,18 @@ __device__ __forceinline__ void pair_tile_coords(int tile, int tiles_m, int tile
   nb = local / gm;
 }
 
-template <typename T, int STAGES, int BNP>
+// kSiluMul: B is a gate/up weight interleaved in blocks of 128 columns
+// ([gate_j | up_j], N = 2I) and the kernel writes act = silu(g) * u ([M, I],
+// through tmC), with both accumulators of row m first multiplied by
+// row_scale[m] when row_scale is given.
+template <typename T, int STAGES, int BNP, bool kSiluMul>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmC, int M, int N, int K, uint32_t idesc) {
+                    const __grid_constant__ CUtensorMap tmC, int M, int N, int K, uint32_t idesc,
+                    const float* __restrict__ row_scale) {
   using L = Tc2Layout<STAGES, BNP>;
   constexpr int kBN = BNP;
+  const int n_out = kSiluMul ? N / 2 : N;  // columns of the output
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -122,6 +128,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_tiles = tiles_m * tiles_n;
   const int kblocks = (K + kBK - 1) / kBK;
 
+  // The next kernel on the stream may start its prologue as SMs free up.
+  pdl_launch_dependents();
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -147,6 +155,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync();  // barriers of both CTAs initialised before any cross-CTA use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Global memory is touched only from here on, once the previous kernel on
+  // the stream has completed (programmatic dependent launch).
+  pdl_wait_prior();
 
   if (warp == 0) {
     // ---------------- TMA producer (both CTAs) ----------------
@@ -264,31 +275,60 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t trow = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                             static_cast<uint32_t>(acc * kBN);
       const int store_y = mb * kBM + static_cast<int>(rank) * kHalf + q * 32;
+      // After this warp's last TMEM load of the tile: hand the accumulator
+      // back on the first CTA's barrier.
+      auto release_if_last = [&](bool last) {
+        if (!last) return;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(map_to_rank(tempty_bar(acc), 0));
+      };
+      // Output chunks of 64 columns: kBN / 64 of C, or (silu_mul) kBN / 128 of
+      // act, each from a 64-column gate chunk and the up chunk 128 columns on.
+      constexpr int kOutChunks = kSiluMul ? kBN / 128 : kBN / 64;
+      const int row = store_y + lane;
+      float rs = 1.f;
+      if (kSiluMul && row_scale != nullptr) rs = row < M ? __ldg(row_scale + row) : 0.f;
 #pragma unroll 1
-      for (int c = 0; c < kBN / 64; ++c) {
-        uint32_t r[64];
-        tmem_ld_32x32b_x32(trow + c * 64, r);
-        tmem_ld_32x32b_x32(trow + c * 64 + 32, r + 32);
-        tmem_wait_ld();
-        if (c == kBN / 64 - 1) {
-          // Accumulator read: release it on the first CTA's barrier.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(map_to_rank(tempty_bar(acc), 0));
+      for (int c = 0; c < kOutChunks; ++c) {
+        float f[64];
+        int store_x;
+        if constexpr (kSiluMul) {
+          // Interleaved weight: tile columns [256 j, 256 j + 256) hold
+          // [gate block | up block] of 128 each.
+          const int gcol = (c / 2) * 256 + (c % 2) * 64;
+          uint32_t g[64], u[64];
+          tmem_ld_32x32b_x32(trow + gcol, g);
+          tmem_ld_32x32b_x32(trow + gcol + 32, g + 32);
+          tmem_ld_32x32b_x32(trow + gcol + 128, u);
+          tmem_ld_32x32b_x32(trow + gcol + 160, u + 32);
+          tmem_wait_ld();
+          release_if_last(c == kOutChunks - 1);
+#pragma unroll
+          for (int j = 0; j < 64; ++j)
+            f[j] = silu_f(__uint_as_float(g[j]) * rs) * (__uint_as_float(u[j]) * rs);
+          store_x = nb * (kBN / 2) + c * 64;
+        } else {
+          uint32_t r[64];
+          tmem_ld_32x32b_x32(trow + c * 64, r);
+          tmem_ld_32x32b_x32(trow + c * 64 + 32, r + 32);
+          tmem_wait_ld();
+          release_if_last(c == kOutChunks - 1);
+#pragma unroll
+          for (int j = 0; j < 64; ++j) f[j] = __uint_as_float(r[j]);
+          store_x = nb * kBN + c * 64;
         }
-        const int store_x = nb * kBN + c * 64;
-        if (store_x >= N || store_y >= M) continue;
+        if (store_x >= n_out || store_y >= M) continue;
         uint32_t pk[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          pk[i] = Elem<T>::pack2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+        for (int i = 0; i < 32; ++i) pk[i] = Elem<T>::pack2(f[2 * i], f[2 * i + 1]);
         const uint32_t buf = cbuf + (nstore & 1) * L::kCBuf;
         if (nstore >= 2 && lane == 0) bulk_wait_read<1>();
         __syncwarp();
-        const uint32_t row = buf + lane * 128;
+        const uint32_t srow = buf + lane * 128;
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-          st_shared_v4(row + ((j ^ (lane & 7)) << 4), pk[4 * j], pk[4 * j + 1], pk[4 * j + 2],
+          st_shared_v4(srow + ((j ^ (lane & 7)) << 4), pk[4 * j], pk[4 * j + 1], pk[4 * j + 2],
                        pk[4 * j + 3]);
         fence_proxy_async_shared();
         __syncwarp();
@@ -318,17 +358,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <typename T, int STAGES, int BNP>
-int launch_tc2(void* c, const void* a, const void* b, int M, int N, int K, bool bf16,
-               cudaStream_t stream, const DeviceInfo& info) {
+template <typename T, int STAGES, int BNP, bool kSiluMul>
+int launch_tc2(void* c, const void* a, const void* b, const float* row_scale, int M, int N, int K,
+               bool bf16, cudaStream_t stream, const DeviceInfo& info) {
   using L = Tc2Layout<STAGES, BNP>;
   constexpr int kBN = BNP;
-  auto kernel = gemm_tc2_kernel<T, STAGES, BNP>;
+  auto kernel = gemm_tc2_kernel<T, STAGES, BNP, kSiluMul>;
   if (int st = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), L::kAlloc, info)) return st;
+  const int n_out = kSiluMul ? N / 2 : N;
   CUtensorMap ta, tb, tc;
   if (int st = make_tmap_2d_16bit(&ta, a, bf16, M, K, K, kBK, kHalf)) return st;
   if (int st = make_tmap_2d_16bit(&tb, b, bf16, K, N, N, 64, kBK)) return st;
-  if (int st = make_tmap_2d_16bit(&tc, c, bf16, M, N, N, 64, 32)) return st;
+  if (int st = make_tmap_2d_16bit(&tc, c, bf16, M, n_out, n_out, 64, 32)) return st;
   const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
   const int max_pairs = info.sm_count / 2;
   const int pairs = tiles < max_pairs ? tiles : max_pairs;
@@ -337,16 +378,20 @@ int launch_tc2(void* c, const void* a, const void* b, int M, int N, int K, bool 
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = L::kAlloc;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // Programmatic dependent launch: the prologue (barrier init, TMEM
+  // allocation, descriptor prefetch) overlaps the previous kernel's tail.
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   // Every MMA is M = 256 (128 rows per CTA) x N = 256.
   const uint32_t idesc = idesc_f16(bf16, kBM, 256, /*a_mn_major=*/false, /*b_mn_major=*/true);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, M, N, K, idesc);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, M, N, K, idesc, row_scale);
   if (e != cudaSuccess)
     return fail(AOTK_ERR_CUDA, "tcgen05 pair gemm launch: %s", cudaGetErrorString(e));
   return check_launch("tcgen05 pair gemm");
@@ -366,8 +411,9 @@ int gemm_tc2(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int m = (int)M, n = (int)N, k = (int)K;
   if (dtype == AOTK_BFLOAT16)
-    return launch_tc2<__nv_bfloat16, kTc2Stages, 256>(c, a, b, m, n, k, true, s, info);
-  return launch_tc2<__half, kTc2Stages, 256>(c, a, b, m, n, k, false, s, info);
+    return launch_tc2<__nv_bfloat16, kTc2Stages, 256, false>(c, a, b, nullptr, m, n, k, true, s,
+                                                             info);
+  return launch_tc2<__half, kTc2Stages, 256, false>(c, a, b, nullptr, m, n, k, false, s, info);
 }
 
 int gemm_tc2_wide(void* c, const void* a, const void* b, int64_t M, int64_t N, int64_t K,
@@ -379,8 +425,35 @@ int gemm_tc2_wide(void* c, const void* a, const void* b, int64_t M, int64_t N, i
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int m = (int)M, n = (int)N, k = (int)K;
   if (dtype == AOTK_BFLOAT16)
-    return launch_tc2<__nv_bfloat16, kTc2WideStages, 512>(c, a, b, m, n, k, true, s, info);
-  return launch_tc2<__half, kTc2WideStages, 512>(c, a, b, m, n, k, false, s, info);
+    return launch_tc2<__nv_bfloat16, kTc2WideStages, 512, false>(c, a, b, nullptr, m, n, k, true,
+                                                                 s, info);
+  return launch_tc2<__half, kTc2WideStages, 512, false>(c, a, b, nullptr, m, n, k, false, s, info);
+}
+
+int gemm_tc2_silu_mul(void* act, const void* a, const void* b, const float* row_scale, int64_t M,
+                      int64_t N2, int64_t K, int dtype, bool wide, void* stream) {
+  DeviceInfo info;
+  if (int st = current_device_info(&info)) return st;
+  if (int st = require_sm100(info)) return st;
+  if (int st = check_tc_preconditions("aotk_gemm_silu_mul", act, a, b, M, N2, K, dtype)) return st;
+  if (N2 % 256 != 0)
+    return fail(AOTK_ERR_UNSUPPORTED,
+                "aotk_gemm_silu_mul: interleaved width 2*I = %lld must be a multiple of 256",
+                (long long)N2);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int m = (int)M, n = (int)N2, k = (int)K;
+  const bool bf16 = dtype == AOTK_BFLOAT16;
+  if (wide) {
+    if (bf16)
+      return launch_tc2<__nv_bfloat16, kTc2WideStages, 512, true>(act, a, b, row_scale, m, n, k,
+                                                                  true, s, info);
+    return launch_tc2<__half, kTc2WideStages, 512, true>(act, a, b, row_scale, m, n, k, false, s,
+                                                         info);
+  }
+  if (bf16)
+    return launch_tc2<__nv_bfloat16, kTc2Stages, 256, true>(act, a, b, row_scale, m, n, k, true, s,
+                                                            info);
+  return launch_tc2<__half, kTc2Stages, 256, true>(act, a, b, row_scale, m, n, k, false, s, info);
 }
 
 int tc2_watchdog(uint32_t* status, bool clear) {

@@ -329,16 +329,25 @@ def test_split_and_whole_schedules_agree():
 # ---- gate/up GEMM fused with silu(gate) * up ----
 
 @pytest.mark.parametrize("shape", [(256, 512, 256), (300, 328, 384), (2560, 1024, 1024),
-                                   (4096, 8192, 3584), (2048, 4096, 3072)], ids=str)
+                                   (4096, 8192, 3584), (2048, 4096, 3072), (1024, 4096, 9472),
+                                   (1000, 4096, 9344), (1000, 4096, 1280)], ids=str)
 def test_gemm_silu_mul_matches_oracle(shape):
     """(M, K, I): interleaved [K, 2I] weight, act [M, I]; the tails of the
     first three run as N halves (each half keeps matching gate and up
-    columns), the last leaves 8 tiles cut along K (fused finalize)."""
+    columns), (4096, 8192, 3584) leaves 8 tiles cut along K (fused finalize);
+    (1024, 4096, 9472) and (1000, 4096, 9344) run on the CTA-pair kernel on
+    256 x 512 tiles (two gate/up block pairs; ragged M, and a last tile whose
+    second pair is past 2I), (1000, 4096, 1280) on 256 x 256 pair tiles."""
     import torch
 
     import aot_kernel
+    from aot_kernel import capi
 
     M, K, inter = shape
+    expect_path = {(1024, 4096, 9472): "tc2_wide", (1000, 4096, 9344): "tc2_wide",
+                   (1000, 4096, 1280): "tc2"}.get(shape)
+    if expect_path:
+        assert capi.gemm_path(M, 2 * inter, K, 148) == expect_path
     a = randn((M, K), M + 1, "bfloat16")
     wg = randn((K, inter), K + 2, "bfloat16", std=K ** -0.5)
     wu = randn((K, inter), K + 3, "bfloat16", std=K ** -0.5)

@@ -223,19 +223,24 @@ def test_rms_rstd_matches_oracle(shape):
 
 
 @pytest.mark.parametrize("shape", [(256, 512, 256), (300, 1024, 384), (2048, 4096, 1792),
-                                   (4096, 8192, 3584)], ids=str)
+                                   (4096, 8192, 3584), (1000, 4096, 9344)], ids=str)
 def test_gemm_silu_mul_folded_norm_matches_oracle(shape):
     """(M, H, I): rms_rstd(x) + gemm_silu_mul(x, fold_norm_weight(W), row_scale)
     against the folded oracle, and against the unfused rms_norm -> gate/up ->
-    silu_mul composition within the GEMM tolerance.  The last shape is the
-    8-way tensor-parallel gate/up of the Llama-70B block (896 tiles: 8 left
-    over, cut along K through the workspace, then row-scaled)."""
+    silu_mul composition within the GEMM tolerance.  (4096, 8192, 3584) is
+    the 8-way tensor-parallel gate/up of the Llama-70B block (896 tiles: 8
+    left over, cut along K through the workspace, then row-scaled); the last
+    runs on the CTA-pair kernel (256 x 512 tiles, the last one half past 2I)."""
     import torch
 
     import aot_kernel
     from tests.conftest import assert_close_for_gemm
 
     M, H, inter = shape
+    if shape == (1000, 4096, 9344):
+        from aot_kernel import capi
+
+        assert capi.gemm_path(M, 2 * inter, H, 148) == "tc2_wide"
     x = randn((M, H), M + 11, "bfloat16")
     nw = randn((H,), H + 12, "bfloat16", mean=1.0, std=0.1)
     wg = randn((H, inter), H + 13, "bfloat16", std=H ** -0.5)
