@@ -74,6 +74,8 @@ CASES = {
     "gemm_m128_down": ("gemm", (128, 14336, 4096)),
     "gate_up_silu_2048": ("gate_up_silu", (2048, 4096, 14336)),
     "tp_gate_up_tp1": ("tp_gate_up", (TOKENS, HIDDEN, INTER)),
+    "tp_gate_up_tp2": ("tp_gate_up", (TOKENS, HIDDEN, INTER // 2)),
+    "tp_gate_up_tp4": ("tp_gate_up", (TOKENS, HIDDEN, INTER // 4)),
     "tp_gate_up_tp8": ("tp_gate_up", (TOKENS, HIDDEN, INTER // 8)),
     "tp_down_tp1": ("gemm", (TOKENS, INTER, HIDDEN)),
     "scaled_gemm_fp8_8192": ("scaled_gemm_e4m3", (8192, 8192, 8192)),
@@ -584,7 +586,7 @@ def gemm_8192(args, peaks: dict) -> dict:
     ms = statistics.mean(s.elapsed_time(e) for s, e in evs)
     tf = 2.0 * n ** 3 / (ms * 1e-3) / 1e12
     return {"ms": round(ms, 4), "tflops": round(tf, 1), "frac": round(tf / peaks["bf16_tflops"], 4),
-            "traffic": traffic_per_launch("gemm_tc_8192")}
+            "traffic": traffic_per_launch("gemm_8192")}
 
 
 def kernel_table(peaks: dict) -> dict:
