@@ -350,10 +350,12 @@ def tp_timed(args, block, x, world: int, peaks: dict, guard) -> dict:
         torch.cuda.synchronize()
         nv1 = clocks.nvlink_kib() if nv0 is not None else None
     total_ms = t0.elapsed_time(t1)
+    down_alone = down_gemm_alone_ms(block, x) if world > 1 else -1.0
     pre = statistics.mean(a.elapsed_time(b) for a, b, _, _ in evs)
     gu_ms = statistics.mean(b.elapsed_time(c) for _, b, c, _ in evs)
     post = statistics.mean(c.elapsed_time(d) for _, _, c, d in evs)
-    total_ms, pre, gu_ms, post = _max_over_ranks([total_ms, pre, gu_ms, post], world)
+    total_ms, pre, gu_ms, post, down_alone = _max_over_ranks([total_ms, pre, gu_ms, post,
+                                                               down_alone], world)
     s = block.shard
     first = "rms_rstd" if s.fold_norm else "rms_norm"
     mid = "gate_up+norm+silu" if s.fold_norm else ("gate_up+silu" if s.fused_silu else "gate_up")
@@ -362,7 +364,8 @@ def tp_timed(args, block, x, world: int, peaks: dict, guard) -> dict:
     achieved = gu_flops / (gu_ms * 1e-3) / 1e12
     return {"ms_per_step": total_ms / args.steps,
             "value": TOKENS * args.steps / (total_ms * 1e-3),
-            "phases_ms": {first: round(pre, 4), mid: round(gu_ms, 4), last: round(post, 4)},
+            "phases_ms": {first: round(pre, 4), mid: round(gu_ms, 4), last: round(post, 4),
+                          **({"down_gemm_alone": round(down_alone, 4)} if world > 1 else {})},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1),
                          "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
                          "frac": round(achieved / peaks["bf16_tflops_sustained"], 4),
@@ -373,6 +376,25 @@ def tp_timed(args, block, x, world: int, peaks: dict, guard) -> dict:
             "gpu_launches": block.launches_per_step() * args.steps,
             "clocks": clocks.summary(),
             "nvlink": nvlink_per_step(nv0, nv1, args.steps, world)}
+
+
+def down_gemm_alone_ms(block, x, reps: int = 10) -> float:
+    """This rank's down projection without the all-reduce (the plain GEMM on
+    the same shard and activations), mean CUDA-event time: what the fused
+    down GEMM + all-reduce would take if the exchange were free."""
+    import torch
+
+    act = block.gate_up_act(x)
+    w = block.shard.w_down
+    for _ in range(2):
+        block.ops.gemm(act, w)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        block.ops.gemm(act, w)
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / reps
 
 
 def nvlink_per_step(nv0, nv1, steps: int, world: int):
