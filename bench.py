@@ -351,11 +351,12 @@ def tp_timed(args, block, x, world: int, peaks: dict, guard) -> dict:
         nv1 = clocks.nvlink_kib() if nv0 is not None else None
     total_ms = t0.elapsed_time(t1)
     down_alone = down_gemm_alone_ms(block, x) if world > 1 else -1.0
+    ar_alone = nccl_allreduce_ms(world) if world > 1 else -1.0
     pre = statistics.mean(a.elapsed_time(b) for a, b, _, _ in evs)
     gu_ms = statistics.mean(b.elapsed_time(c) for _, b, c, _ in evs)
     post = statistics.mean(c.elapsed_time(d) for _, _, c, d in evs)
-    total_ms, pre, gu_ms, post, down_alone = _max_over_ranks([total_ms, pre, gu_ms, post,
-                                                               down_alone], world)
+    total_ms, pre, gu_ms, post, down_alone, ar_alone = _max_over_ranks(
+        [total_ms, pre, gu_ms, post, down_alone, ar_alone], world)
     s = block.shard
     first = "rms_rstd" if s.fold_norm else "rms_norm"
     mid = "gate_up+norm+silu" if s.fold_norm else ("gate_up+silu" if s.fused_silu else "gate_up")
@@ -365,7 +366,8 @@ def tp_timed(args, block, x, world: int, peaks: dict, guard) -> dict:
     return {"ms_per_step": total_ms / args.steps,
             "value": TOKENS * args.steps / (total_ms * 1e-3),
             "phases_ms": {first: round(pre, 4), mid: round(gu_ms, 4), last: round(post, 4),
-                          **({"down_gemm_alone": round(down_alone, 4)} if world > 1 else {})},
+                          **({"down_gemm_alone": round(down_alone, 4),
+                              "nccl_all_reduce_alone": round(ar_alone, 4)} if world > 1 else {})},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1),
                          "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
                          "frac": round(achieved / peaks["bf16_tflops_sustained"], 4),
@@ -394,6 +396,27 @@ def down_gemm_alone_ms(block, x, reps: int = 10) -> float:
         block.ops.gemm(act, w)
     e.record()
     torch.cuda.synchronize()
+    return s.elapsed_time(e) / reps
+
+
+def nccl_allreduce_ms(world: int, reps: int = 10) -> float:
+    """One NCCL all-reduce (sum) of the block's [4096, 8192] bf16 output on
+    its own, mean CUDA-event time: the box's collective speed for the same
+    bytes, beside the fused kernel (every rank takes part)."""
+    import torch
+    import torch.distributed as dist
+
+    t = torch.zeros((TOKENS, HIDDEN), dtype=torch.bfloat16, device="cuda")
+    for _ in range(2):
+        dist.all_reduce(t)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        dist.all_reduce(t)
+    e.record()
+    torch.cuda.synchronize()
+    del t
     return s.elapsed_time(e) / reps
 
 
