@@ -124,9 +124,31 @@ def load_peaks() -> tuple[dict, str]:
 
 # ---------------------------------------------------------------- clocks
 
+# The sampling loop runs in a child process: NVML queries take milliseconds
+# and, in the process that launches the kernels, stall its launches; with the
+# ranks of a tensor-parallel step coupled through the all-reduce, a stall on
+# any rank idles all of them.
+_SAMPLER_CHILD = r"""
+import sys, time, pynvml
+pynvml.nvmlInit()
+h = pynvml.nvmlDeviceGetHandleByPciBusId(sys.argv[1].encode())
+period = float(sys.argv[2])
+while True:
+    try:
+        sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+        pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+        rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+        print(f"{sm},{pw},{rs}", flush=True)
+    except pynvml.NVMLError:
+        pass
+    time.sleep(period)
+"""
+
+
 class ClockSampler:
     """Samples this rank's GPU clock, power and clock-event reasons through NVML
-    (read-only queries) every 10 ms while the timed region runs."""
+    (read-only queries) every 10 ms while the timed region runs, from a child
+    process (``_SAMPLER_CHILD``)."""
 
     REASONS = {"hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
                "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
@@ -138,9 +160,9 @@ class ClockSampler:
         self.device, self.period = device, period_s
         self.samples: list[tuple[float, float, int]] = []
         self.max_mhz = None
-        self._stop = None
-        self._thread = None
+        self._proc = None
         self._nvml = None
+        self._bus_id = None
 
     def _handle(self):
         import pynvml
@@ -149,26 +171,12 @@ class ClockSampler:
         pynvml.nvmlInit()
         p = torch.cuda.get_device_properties(self.device)
         # torch reports the PCI location as integers; NVML wants "DDDDDDDD:BB:DD.0".
-        bus_id = f"{int(p.pci_domain_id):08X}:{int(p.pci_bus_id):02X}:{int(p.pci_device_id):02X}.0"
-        try:
-            return pynvml.nvmlDeviceGetHandleByPciBusId(bus_id.encode())
-        except pynvml.NVMLError:
-            return pynvml.nvmlDeviceGetHandleByIndex(self.device)
-
-    def _run(self, h):
-        nv = self._nvml
-        while not self._stop.is_set():
-            try:
-                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
-                pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
-                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
-                self.samples.append((float(sm), pw, int(rs)))
-            except Exception:  # noqa: BLE001
-                pass
-            self._stop.wait(self.period)
+        self._bus_id = (f"{int(p.pci_domain_id):08X}:{int(p.pci_bus_id):02X}:"
+                        f"{int(p.pci_device_id):02X}.0")
+        return pynvml.nvmlDeviceGetHandleByPciBusId(self._bus_id.encode())
 
     def __enter__(self):
-        import threading
+        import subprocess
 
         try:
             import pynvml
@@ -176,18 +184,35 @@ class ClockSampler:
             self._nvml = pynvml
             h = self._handle()
             self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            self._proc = subprocess.Popen(
+                [sys.executable, "-c", _SAMPLER_CHILD, self._bus_id, str(self.period)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            # Sampling has begun once the child's first line arrives.
+            import select
+
+            if select.select([self._proc.stdout], [], [], 30.0)[0]:
+                self._keep(self._proc.stdout.readline())
         except Exception:  # noqa: BLE001
             self._nvml = None
-            return self
-        self._stop = threading.Event()
-        self._thread = threading.Thread(target=self._run, args=(h,), daemon=True)
-        self._thread.start()
         return self
 
+    def _keep(self, line: str) -> None:
+        try:
+            sm, pw, rs = line.split(",")
+            self.samples.append((float(sm), float(pw), int(rs)))
+        except ValueError:
+            pass
+
     def __exit__(self, *exc):
-        if self._thread is not None:
-            self._stop.set()
-            self._thread.join(timeout=5)
+        if self._proc is not None:
+            self._proc.terminate()  # this sampler's own child, by its PID
+            try:
+                out, _ = self._proc.communicate(timeout=10)
+            except Exception:  # noqa: BLE001
+                self._proc.kill()
+                out, _ = self._proc.communicate()
+            for line in (out or "").splitlines():
+                self._keep(line)
         return False
 
     def nvlink_kib(self):
@@ -337,9 +362,9 @@ def tp_timed(args, block, x, world: int, peaks: dict, guard) -> dict:
     # meet, so that every rank enters the timed steps at the same moment.
     with ClockSampler(torch.cuda.current_device()) as clocks:
         evs = [(ev(), ev(), ev(), ev()) for _ in range(args.steps)]
+        nv0 = clocks.nvlink_kib() if world > 1 else None
         _meet(world)
         guard.check()
-        nv0 = clocks.nvlink_kib() if world > 1 else None
         t0, t1 = ev(), ev()
         t0.record()
         for a, b, c, d in evs:
