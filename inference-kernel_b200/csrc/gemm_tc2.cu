@@ -89,6 +89,26 @@ __device__ __forceinline__ void pair_tile_coords(int tile, int tiles_m, int tile
   nb = local / gm;
 }
 
+// Work item i of a pair: its whole tiles (tile < tail_begin, round robin
+// over the pairs), then at most one half of a tail tile (half = 0 or 1, N
+// columns [128 half, 128 half + 128) of a 256-column tile, or for silu_mul
+// the matching 64 gate and 64 up columns).  Without a cut tail, tail_begin
+// equals the tile count.
+__device__ __forceinline__ bool pair_item(int i, int pair, int num_pairs, int num_tiles,
+                                          int tail_begin, int& tile, int& half) {
+  const int whole = tail_begin > pair ? (tail_begin - pair + num_pairs - 1) / num_pairs : 0;
+  if (i < whole) {
+    tile = pair + i * num_pairs;
+    half = -1;
+    return true;
+  }
+  const int u = pair + (i - whole) * num_pairs;
+  if (u >= 2 * (num_tiles - tail_begin)) return false;
+  tile = tail_begin + u / 2;
+  half = u % 2;
+  return true;
+}
+
 // kSiluMul: B is a gate/up weight interleaved in blocks of 128 columns
 // ([gate_j | up_j], N = 2I) and the kernel writes act = silu(g) * u ([M, I],
 // through tmC), with both accumulators of row m first multiplied by
@@ -97,7 +117,7 @@ template <typename T, int STAGES, int BNP, bool kSiluMul>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmC, int M, int N, int K, uint32_t idesc,
-                    const float* __restrict__ row_scale) {
+                    const float* __restrict__ row_scale, int tail_begin) {
   using L = Tc2Layout<STAGES, BNP>;
   constexpr int kBN = BNP;
   const int n_out = kSiluMul ? N / 2 : N;  // columns of the output
@@ -127,6 +147,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tiles_n = (N + kBN - 1) / kBN;
   const int num_tiles = tiles_m * tiles_n;
   const int kblocks = (K + kBK - 1) / kBK;
+  // A half tail item is one MMA of N = 128 per K step.
+  const uint32_t idesc_half = (idesc & ~(0x3Fu << 17)) | ((128u >> 3) << 17);
 
   // The next kernel on the stream may start its prologue as SMs free up.
   pdl_launch_dependents();
@@ -166,7 +188,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
+      int tile, half;
+      for (int i = 0; ok && pair_item(i, pair, num_pairs, num_tiles, tail_begin, tile, half);
+           ++i) {
         int mb, nb;
         pair_tile_coords(tile, tiles_m, tiles_n, mb, nb);
         const int row0 = mb * kBM + static_cast<int>(rank) * kHalf;
@@ -177,15 +201,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           // The stage's bytes are counted on the first CTA's full barrier.
           const uint32_t fb = map_to_rank(full_bar(stage), 0);
-          if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), L::kPairStageBytes);
+          if (rank == 0)
+            mbar_arrive_expect_tx(full_bar(stage), half < 0 ? L::kPairStageBytes
+                                                            : 2 * (L::kABytes + L::kBBox));
           tma_load_2d_pair(sA + stage * L::kABytes, &tmA, kb * kBK, row0, fb);
-          // Box j feeds MMA j / 2 (columns [256 h, 256 h + 256) of the tile),
-          // of which this CTA stages the half [128 rank, 128 rank + 128).
+          if (half < 0) {
+            // Box j feeds MMA j / 2 (columns [256 h, 256 h + 256) of the
+            // tile), of which this CTA stages [128 rank, 128 rank + 128).
 #pragma unroll
-          for (int j = 0; j < L::kBBoxes; ++j)
-            tma_load_2d_pair(sB + stage * L::kBBytes + j * L::kBBox, &tmB,
-                             nb * kBN + (j / 2) * 256 + static_cast<int>(rank) * kHalf + (j % 2) * 64,
-                             kb * kBK, fb);
+            for (int j = 0; j < L::kBBoxes; ++j)
+              tma_load_2d_pair(
+                  sB + stage * L::kBBytes + j * L::kBBox, &tmB,
+                  nb * kBN + (j / 2) * 256 + static_cast<int>(rank) * kHalf + (j % 2) * 64,
+                  kb * kBK, fb);
+          } else {
+            // One 64-column box per CTA: columns [128 half + 64 rank, +64),
+            // or for silu_mul gate (rank 0) / up (rank 1) columns 64 half on.
+            const int col = kSiluMul ? nb * kBN + static_cast<int>(rank) * 128 + half * 64
+                                     : nb * kBN + half * 128 + static_cast<int>(rank) * 64;
+            tma_load_2d_pair(sB + stage * L::kBBytes, &tmB, col, kb * kBK, fb);
+          }
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -215,7 +250,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
+      int tile, half;
+      for (int i = 0; ok && pair_item(i, pair, num_pairs, num_tiles, tail_begin, tile, half);
+           ++i) {
         if (!mbar_wait_bounded(tempty_bar(acc), acc_phase ^ 1u, abort_flag, wd, kWdMma)) {
           ok = false;
           break;
@@ -233,11 +270,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < kBK / kUmmaK; ++k) {
             const uint64_t ad = sdesc_sw128(a0 + k * kUmmaK * 2, 16, 1024);
+            if (half < 0) {
 #pragma unroll
-            for (int h = 0; h < L::kMmas; ++h) {
-              const uint64_t bd =
-                  sdesc_sw128(b0 + h * 2 * L::kBBox + k * kUmmaK * 128, L::kBBox, 1024);
-              umma_f16_pair(d_tmem + h * 256, ad, bd, idesc, kb > 0 || k > 0);
+              for (int h = 0; h < L::kMmas; ++h) {
+                const uint64_t bd =
+                    sdesc_sw128(b0 + h * 2 * L::kBBox + k * kUmmaK * 128, L::kBBox, 1024);
+                umma_f16_pair(d_tmem + h * 256, ad, bd, idesc, kb > 0 || k > 0);
+              }
+            } else {
+              const uint64_t bd = sdesc_sw128(b0 + k * kUmmaK * 128, L::kBBox, 1024);
+              umma_f16_pair(d_tmem, ad, bd, idesc_half, kb > 0 || k > 0);
             }
           }
           umma_commit_pair(empty_bar(stage), 0x3);
@@ -264,7 +306,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     int nstore = 0;
-    for (int tile = pair; tile < num_tiles; tile += num_pairs) {
+    int tile, half;
+    for (int i = 0; pair_item(i, pair, num_pairs, num_tiles, tail_begin, tile, half); ++i) {
       int mb, nb;
       pair_tile_coords(tile, tiles_m, tiles_n, mb, nb);
       int ok = 1;
@@ -285,38 +328,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       // Output chunks of 64 columns: kBN / 64 of C, or (silu_mul) kBN / 128 of
       // act, each from a 64-column gate chunk and the up chunk 128 columns on.
-      constexpr int kOutChunks = kSiluMul ? kBN / 128 : kBN / 64;
+      // A half item holds 128 accumulator columns: two chunks of C, or one
+      // act chunk from gate columns [0, 64) and up columns [64, 128).
+      const int out_chunks =
+          half >= 0 ? (kSiluMul ? 1 : 2) : (kSiluMul ? kBN / 128 : kBN / 64);
       const int row = store_y + lane;
       float rs = 1.f;
       if (kSiluMul && row_scale != nullptr) rs = row < M ? __ldg(row_scale + row) : 0.f;
 #pragma unroll 1
-      for (int c = 0; c < kOutChunks; ++c) {
+      for (int c = 0; c < out_chunks; ++c) {
         float f[64];
         int store_x;
         if constexpr (kSiluMul) {
           // Interleaved weight: tile columns [256 j, 256 j + 256) hold
           // [gate block | up block] of 128 each.
-          const int gcol = (c / 2) * 256 + (c % 2) * 64;
+          const int gcol = half >= 0 ? 0 : (c / 2) * 256 + (c % 2) * 64;
+          const int ucol = half >= 0 ? 64 : gcol + 128;
           uint32_t g[64], u[64];
           tmem_ld_32x32b_x32(trow + gcol, g);
           tmem_ld_32x32b_x32(trow + gcol + 32, g + 32);
-          tmem_ld_32x32b_x32(trow + gcol + 128, u);
-          tmem_ld_32x32b_x32(trow + gcol + 160, u + 32);
+          tmem_ld_32x32b_x32(trow + ucol, u);
+          tmem_ld_32x32b_x32(trow + ucol + 32, u + 32);
           tmem_wait_ld();
-          release_if_last(c == kOutChunks - 1);
+          release_if_last(c == out_chunks - 1);
 #pragma unroll
           for (int j = 0; j < 64; ++j)
             f[j] = silu_f(__uint_as_float(g[j]) * rs) * (__uint_as_float(u[j]) * rs);
-          store_x = nb * (kBN / 2) + c * 64;
+          store_x = nb * (kBN / 2) + (half >= 0 ? half * 64 : c * 64);
         } else {
           uint32_t r[64];
           tmem_ld_32x32b_x32(trow + c * 64, r);
           tmem_ld_32x32b_x32(trow + c * 64 + 32, r + 32);
           tmem_wait_ld();
-          release_if_last(c == kOutChunks - 1);
+          release_if_last(c == out_chunks - 1);
 #pragma unroll
           for (int j = 0; j < 64; ++j) f[j] = __uint_as_float(r[j]);
-          store_x = nb * kBN + c * 64;
+          store_x = nb * kBN + (half >= 0 ? half * 128 : 0) + c * 64;
         }
         if (store_x >= n_out || store_y >= M) continue;
         uint32_t pk[32];
@@ -372,7 +419,16 @@ int launch_tc2(void* c, const void* a, const void* b, const float* row_scale, in
   if (int st = make_tmap_2d_16bit(&tc, c, bf16, M, n_out, n_out, 64, 32)) return st;
   const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
   const int max_pairs = info.sm_count / 2;
-  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  int pairs = tiles < max_pairs ? tiles : max_pairs;
+  int tail_begin = tiles;
+  // 256-column tiles: a partial last round of at most half the pairs is cut
+  // into N halves (twice the pairs, half a tile each).
+  const int full = tiles / max_pairs;
+  const int rem = tiles - full * max_pairs;
+  if (BNP == 256 && rem > 0 && 2 * rem <= max_pairs) {
+    pairs = full > 0 ? max_pairs : 2 * rem;
+    tail_begin = full * max_pairs;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -391,7 +447,8 @@ int launch_tc2(void* c, const void* a, const void* b, const float* row_scale, in
   cfg.numAttrs = 2;
   // Every MMA is M = 256 (128 rows per CTA) x N = 256.
   const uint32_t idesc = idesc_f16(bf16, kBM, 256, /*a_mn_major=*/false, /*b_mn_major=*/true);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, M, N, K, idesc, row_scale);
+  cudaError_t e =
+      cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, M, N, K, idesc, row_scale, tail_begin);
   if (e != cudaSuccess)
     return fail(AOTK_ERR_CUDA, "tcgen05 pair gemm launch: %s", cudaGetErrorString(e));
   return check_launch("tcgen05 pair gemm");

@@ -106,7 +106,10 @@ def test_capi_gemm_tc(shape, dt):
     assert capi.watchdog_status() == 0
 
 
-@pytest.mark.parametrize("shape", TC_SHAPES + [(256, 64, 256), (8192, 1024, 2048)], ids=str)
+# Most of these leave a last round of at most 37 pair tiles (or are a single
+# such round), which the kernel cuts into N halves.
+@pytest.mark.parametrize("shape", TC_SHAPES + [(256, 64, 256), (8192, 1024, 2048),
+                                               (1024, 512, 4864), (1000, 512, 4856)], ids=str)
 @pytest.mark.parametrize("dt", ["bfloat16", "float16"])
 def test_capi_gemm_tc2(shape, dt):
     from aot_kernel import capi
@@ -330,14 +333,17 @@ def test_split_and_whole_schedules_agree():
 
 @pytest.mark.parametrize("shape", [(256, 512, 256), (300, 328, 384), (2560, 1024, 1024),
                                    (4096, 8192, 3584), (2048, 4096, 3072), (1024, 4096, 9472),
-                                   (1000, 4096, 9344), (1000, 4096, 1280)], ids=str)
+                                   (1000, 4096, 9344), (1000, 4096, 1280), (1000, 4096, 1024)],
+                         ids=str)
 def test_gemm_silu_mul_matches_oracle(shape):
     """(M, K, I): interleaved [K, 2I] weight, act [M, I]; the tails of the
     first three run as N halves (each half keeps matching gate and up
     columns), (4096, 8192, 3584) leaves 8 tiles cut along K (fused finalize);
     (1024, 4096, 9472) and (1000, 4096, 9344) run on the CTA-pair kernel on
     256 x 512 tiles (two gate/up block pairs; ragged M, and a last tile whose
-    second pair is past 2I), (1000, 4096, 1280) on 256 x 256 pair tiles."""
+    second pair is past 2I), (1000, 4096, 1280) on 256 x 256 pair tiles, and
+    (1000, 4096, 1024) on 256 x 256 pair tiles cut into N halves (32 tiles
+    on 64 pairs: gate and up quarters stay together)."""
     import torch
 
     import aot_kernel
@@ -345,7 +351,7 @@ def test_gemm_silu_mul_matches_oracle(shape):
 
     M, K, inter = shape
     expect_path = {(1024, 4096, 9472): "tc2_wide", (1000, 4096, 9344): "tc2_wide",
-                   (1000, 4096, 1280): "tc2"}.get(shape)
+                   (1000, 4096, 1280): "tc2", (1000, 4096, 1024): "tc2"}.get(shape)
     if expect_path:
         assert capi.gemm_path(M, 2 * inter, K, 148) == expect_path
     a = randn((M, K), M + 1, "bfloat16")
