@@ -190,7 +190,7 @@ class ClockSampler:
             # Sampling has begun once the child's first line arrives.
             import select
 
-            if select.select([self._proc.stdout], [], [], 30.0)[0]:
+            if select.select([self._proc.stdout], [], [], 10.0)[0]:
                 self._keep(self._proc.stdout.readline())
         except Exception:  # noqa: BLE001
             self._nvml = None
