@@ -16,6 +16,7 @@
 // normalises h, all in the same pass: x and residual are read once, h and y
 // written once.
 #include "common.h"
+#include "sm100.cuh"
 #include "vec.cuh"
 
 namespace aotk {
@@ -64,6 +65,11 @@ __global__ void __launch_bounds__(TPR > kBlock ? TPR : kBlock)
   const int64_t groups = (rows + RPB - 1) / RPB;
   const uint4* wr = reinterpret_cast<const uint4*>(w);
 
+  // Programmatic dependent launch: the next kernel may start its prologue
+  // now; x (and the residual) may come from the previous kernel, so nothing
+  // is read before it has completed.
+  sm100::pdl_launch_dependents();
+  sm100::pdl_wait_prior();
   uint4 cur[VPT], cur_r[kRes ? VPT : 1];
   int64_t g = blockIdx.x;
   load_row<T, VPT, TPR>(x, g * RPB + sub, rows, cols, t, cur);
@@ -191,7 +197,18 @@ int launch_vec(const T* x, const T* r, const T* w, T* y, T* h, int64_t rows, int
   const int64_t groups = (rows + RPB - 1) / RPB;
   const int64_t capacity = (int64_t)per_sm * info.sm_count;
   const int64_t blocks = groups < capacity ? groups : capacity;
-  kernel<<<(unsigned)blocks, THREADS, 0, s>>>(x, r, w, y, h, rows, cols, eps, stats);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)blocks, 1, 1);
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, x, r, w, y, h, rows, cols, eps, stats);
+  if (e != cudaSuccess)
+    return fail(AOTK_ERR_CUDA, "aotk_rmsnorm_forward launch: %s", cudaGetErrorString(e));
   return check_launch("aotk_rmsnorm_forward");
 }
 
