@@ -6,8 +6,13 @@
 // UNROLL * 16 bytes per thread are in flight, and walks the tensor with a
 // grid-stride loop over a grid of exactly one wave of resident blocks.  The reference runs one
 // scalar element per thread with 458 752 blocks at [8192, 14336]
-// (aot_kernel/csrc/activation/silu.cu:14-19, :29-39).
+// (aot_kernel/csrc/activation/silu.cu:14-19, :29-39).  Every kernel here is
+// launched with programmatic dependent launch: it lets the next kernel on the
+// stream start its prologue at once, and touches global memory only after
+// griddepcontrol.wait, so its own launch and setup overlap the tail of the
+// kernel before it.
 #include "common.h"
+#include "sm100.cuh"
 #include "vec.cuh"
 
 #include <mutex>
@@ -32,6 +37,8 @@ template <typename T, typename Op>
 __global__ void __launch_bounds__(kThreads) unary_vec_kernel(const uint4* __restrict__ x,
                                                              uint4* __restrict__ y, int64_t n_vec) {
   constexpr int E = Elem<T>::kPerVec;
+  sm100::pdl_launch_dependents();
+  sm100::pdl_wait_prior();
   const int64_t step = (int64_t)gridDim.x * kThreads * kUnroll;
   for (int64_t base = (int64_t)blockIdx.x * kThreads * kUnroll + threadIdx.x; base < n_vec;
        base += step) {
@@ -59,6 +66,8 @@ __global__ void __launch_bounds__(kThreads) unary_vec_kernel(const uint4* __rest
 template <typename T, typename Op>
 __global__ void __launch_bounds__(kThreads) unary_scalar_kernel(const T* __restrict__ x,
                                                                 T* __restrict__ y, int64_t n) {
+  sm100::pdl_launch_dependents();
+  sm100::pdl_wait_prior();
   const int64_t step = (int64_t)gridDim.x * kThreads;
   for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n; i += step) {
     y[i] = Elem<T>::from_f(Op::apply(Elem<T>::to_f(x[i])));
@@ -73,6 +82,8 @@ __global__ void __launch_bounds__(kThreads) silu_mul_vec_kernel(
     T* __restrict__ out, int64_t out_stride, int64_t rows, int64_t vec_per_row) {
   constexpr int E = Elem<T>::kPerVec;
   const int64_t n_vec = rows * vec_per_row;
+  sm100::pdl_launch_dependents();
+  sm100::pdl_wait_prior();
   const int64_t step = (int64_t)gridDim.x * kThreads * kUnroll;
   for (int64_t base = (int64_t)blockIdx.x * kThreads * kUnroll + threadIdx.x; base < n_vec;
        base += step) {
@@ -109,6 +120,8 @@ __global__ void __launch_bounds__(kThreads) silu_mul_scalar_kernel(
     const T* __restrict__ gate, int64_t gate_stride, const T* __restrict__ up, int64_t up_stride,
     T* __restrict__ out, int64_t out_stride, int64_t rows, int64_t cols) {
   const int64_t n = rows * cols;
+  sm100::pdl_launch_dependents();
+  sm100::pdl_wait_prior();
   const int64_t step = (int64_t)gridDim.x * kThreads;
   for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n; i += step) {
     const int64_t r = i / cols;
@@ -148,6 +161,25 @@ int grid_for(const void* kernel, int64_t work_items, int per_block, const Device
   return (int)(want < cap ? (want > 0 ? want : 1) : cap);
 }
 
+// Launches `kernel` on `grid` blocks of kThreads with programmatic stream
+// serialisation and turns a launch error into AOTK_ERR_CUDA.
+template <typename... Params, typename... Args>
+int launch_pdl(void (*kernel)(Params...), int grid, cudaStream_t stream, const char* name,
+               Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+  if (e != cudaSuccess) return fail(AOTK_ERR_CUDA, "%s launch: %s", name, cudaGetErrorString(e));
+  return check_launch(name);
+}
+
 template <typename T, typename Op>
 int launch_unary(void* out, const void* x, int64_t n, cudaStream_t stream, const char* name) {
   DeviceInfo info;
@@ -158,19 +190,20 @@ int launch_unary(void* out, const void* x, int64_t n, cudaStream_t stream, const
     const int64_t n_vec = n / E;
     if (n_vec > 0) {
       auto kernel = unary_vec_kernel<T, Op>;
-      kernel<<<grid_for(reinterpret_cast<const void*>(kernel), n_vec, kThreads * kUnroll, info),
-               kThreads, 0, stream>>>(static_cast<const uint4*>(x), static_cast<uint4*>(out),
-                                      n_vec);
-      if (int st = check_launch(name)) return st;
+      const int grid = grid_for(reinterpret_cast<const void*>(kernel), n_vec, kThreads * kUnroll, info);
+      if (int st = launch_pdl(kernel, grid, stream, name, static_cast<const uint4*>(x),
+                              static_cast<uint4*>(out), n_vec))
+        return st;
     }
     head = n_vec * E;
   }
   const int64_t tail = n - head;
   if (tail > 0) {
     auto kernel = unary_scalar_kernel<T, Op>;
-    kernel<<<grid_for(reinterpret_cast<const void*>(kernel), tail, kThreads, info), kThreads, 0,
-             stream>>>(static_cast<const T*>(x) + head, static_cast<T*>(out) + head, tail);
-    if (int st = check_launch(name)) return st;
+    const int grid = grid_for(reinterpret_cast<const void*>(kernel), tail, kThreads, info);
+    if (int st = launch_pdl(kernel, grid, stream, name, static_cast<const T*>(x) + head,
+                            static_cast<T*>(out) + head, tail))
+      return st;
   }
   return AOTK_OK;
 }
@@ -201,17 +234,17 @@ int launch_silu_mul(void* out, int64_t out_stride, const void* gate, int64_t gat
   if (vec_ok) {
     const int64_t vpr = cols / E;
     auto kernel = silu_mul_vec_kernel<T>;
-    kernel<<<grid_for(reinterpret_cast<const void*>(kernel), rows * vpr, kThreads * kUnroll, info),
-             kThreads, 0, stream>>>(static_cast<const T*>(gate), gate_stride,
-                                    static_cast<const T*>(up), up_stride, static_cast<T*>(out),
-                                    out_stride, rows, vpr);
-  } else {
-    auto kernel = silu_mul_scalar_kernel<T>;
-    kernel<<<grid_for(reinterpret_cast<const void*>(kernel), rows * cols, kThreads, info), kThreads,
-             0, stream>>>(static_cast<const T*>(gate), gate_stride, static_cast<const T*>(up),
-                          up_stride, static_cast<T*>(out), out_stride, rows, cols);
+    const int grid =
+        grid_for(reinterpret_cast<const void*>(kernel), rows * vpr, kThreads * kUnroll, info);
+    return launch_pdl(kernel, grid, stream, "aotk_silu_mul_forward", static_cast<const T*>(gate),
+                      gate_stride, static_cast<const T*>(up), up_stride, static_cast<T*>(out),
+                      out_stride, rows, vpr);
   }
-  return check_launch("aotk_silu_mul_forward");
+  auto kernel = silu_mul_scalar_kernel<T>;
+  const int grid = grid_for(reinterpret_cast<const void*>(kernel), rows * cols, kThreads, info);
+  return launch_pdl(kernel, grid, stream, "aotk_silu_mul_forward", static_cast<const T*>(gate),
+                    gate_stride, static_cast<const T*>(up), up_stride, static_cast<T*>(out),
+                    out_stride, rows, cols);
 }
 
 }  // namespace
