@@ -97,9 +97,9 @@ int check_tc_preconditions(const char* who, const void* c, const void* a, const 
 // tiles over all SMs, its partial last wave cut into N halves or K splits by
 // plan_tc) and the CTA-pair kernel on 256 x 256 or 256 x 512 tiles (over SM
 // pairs).  Time is counted in rounds of 128 x 256 x K work per SM; a 256 x 256
-// pair tile is one such unit per SM, a 256 x 512 one two; both the 1-CTA and
-// the 256 x 256 pair kernel cut a partial last round of at most half their
-// slots into N halves.  The pair kernels'
+// pair tile is one such unit per SM, a 256 x 512 one two; all three kernels
+// cut a partial last round of at most half their slots into N halves.  The
+// pair kernels'
 // throughput advantage on whole rounds is what was measured on B200 with each
 // kernel running back to back for 0.6 s at the 1 kW power cap (as GEMMs run
 // inside a model step): 256 x 256 1.04-1.08x, 256 x 512 1.07-1.10x the 1-CTA
@@ -122,14 +122,13 @@ int gemm_opt_path(int64_t M, int64_t N, int64_t K, int sm_count, bool with_works
   if (sch[4]) tc += 0.6;                    // last wave as N halves
   else if (sch[5] > 1) tc += 0.35;          // last wave as K splits
   const int64_t pairs = sm_count / 2;
-  auto rounds = [&](int64_t tiles) { return static_cast<double>((tiles + pairs - 1) / pairs); };
-  // 256 x 256 pair tiles: a last round of at most half the pairs runs as N
+  // Rounds of pair tiles: a last round of at most half the pairs runs as N
   // halves (charged 0.6 of a round, as for the 1-CTA kernel).
-  const int64_t t2 = ((M + 255) / 256) * ((N + 255) / 256);
-  const int64_t r2 = t2 % pairs;
-  const double pair =
-      (static_cast<double>(t2 / pairs) + (r2 == 0 ? 0.0 : (2 * r2 <= pairs ? 0.6 : 1.0))) /
-      kPairGain;
+  auto rounds = [&](int64_t tiles) {
+    const int64_t rem = tiles % pairs;
+    return static_cast<double>(tiles / pairs) + (rem == 0 ? 0.0 : (2 * rem <= pairs ? 0.6 : 1.0));
+  };
+  const double pair = rounds(((M + 255) / 256) * ((N + 255) / 256)) / kPairGain;
   const double wide = 2.0 * rounds(((M + 255) / 256) * ((N + 511) / 512)) / kWideGain;
   if (wide <= pair && wide < kMargin * tc) return AOTK_PATH_TC2_WIDE;
   if (pair < wide && pair < kMargin * tc) return AOTK_PATH_TC2;

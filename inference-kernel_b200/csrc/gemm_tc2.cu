@@ -91,8 +91,9 @@ __device__ __forceinline__ void pair_tile_coords(int tile, int tiles_m, int tile
 
 // Work item i of a pair: its whole tiles (tile < tail_begin, round robin
 // over the pairs), then at most one half of a tail tile (half = 0 or 1, N
-// columns [128 half, 128 half + 128) of a 256-column tile, or for silu_mul
-// the matching 64 gate and 64 up columns).  Without a cut tail, tail_begin
+// columns [BNP/2 half, BNP/2 half + BNP/2) of the tile; for silu_mul the
+// matching gate and up columns: 64 + 64 of a 256-column tile, one whole
+// [gate | up] block of a 512-column tile).  Without a cut tail, tail_begin
 // equals the tile count.
 __device__ __forceinline__ bool pair_item(int i, int pair, int num_pairs, int num_tiles,
                                           int tail_begin, int& tile, int& half) {
@@ -147,8 +148,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tiles_n = (N + kBN - 1) / kBN;
   const int num_tiles = tiles_m * tiles_n;
   const int kblocks = (K + kBK - 1) / kBK;
-  // A half tail item is one MMA of N = 128 per K step.
-  const uint32_t idesc_half = (idesc & ~(0x3Fu << 17)) | ((128u >> 3) << 17);
+  // A half tail item is one MMA per K step: N = 128 for 256-column tiles,
+  // N = 256 (the tile's first MMA) for 512-column tiles.
+  const uint32_t idesc_half =
+      BNP == 256 ? (idesc & ~(0x3Fu << 17)) | ((128u >> 3) << 17) : idesc;
 
   // The next kernel on the stream may start its prologue as SMs free up.
   pdl_launch_dependents();
@@ -202,8 +205,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           // The stage's bytes are counted on the first CTA's full barrier.
           const uint32_t fb = map_to_rank(full_bar(stage), 0);
           if (rank == 0)
-            mbar_arrive_expect_tx(full_bar(stage), half < 0 ? L::kPairStageBytes
-                                                            : 2 * (L::kABytes + L::kBBox));
+            mbar_arrive_expect_tx(full_bar(stage),
+                                  half < 0 ? L::kPairStageBytes
+                                           : 2 * (L::kABytes + (L::kBBoxes / 2) * L::kBBox));
           tma_load_2d_pair(sA + stage * L::kABytes, &tmA, kb * kBK, row0, fb);
           if (half < 0) {
             // Box j feeds MMA j / 2 (columns [256 h, 256 h + 256) of the
@@ -214,12 +218,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                   sB + stage * L::kBBytes + j * L::kBBox, &tmB,
                   nb * kBN + (j / 2) * 256 + static_cast<int>(rank) * kHalf + (j % 2) * 64,
                   kb * kBK, fb);
-          } else {
+          } else if constexpr (BNP == 256) {
             // One 64-column box per CTA: columns [128 half + 64 rank, +64),
             // or for silu_mul gate (rank 0) / up (rank 1) columns 64 half on.
             const int col = kSiluMul ? nb * kBN + static_cast<int>(rank) * 128 + half * 64
                                      : nb * kBN + half * 128 + static_cast<int>(rank) * 64;
             tma_load_2d_pair(sB + stage * L::kBBytes, &tmB, col, kb * kBK, fb);
+          } else {
+            // The boxes of MMA `half` alone: columns [256 half, 256 half +
+            // 256) of the tile (for silu_mul one [gate | up] block), of which
+            // this CTA stages [128 rank, 128 rank + 128).
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+              tma_load_2d_pair(sB + stage * L::kBBytes + j * L::kBBox, &tmB,
+                               nb * kBN + half * 256 + static_cast<int>(rank) * kHalf + j * 64,
+                               kb * kBK, fb);
           }
           ++issued;
           if (++stage == STAGES) {
@@ -328,10 +341,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       // Output chunks of 64 columns: kBN / 64 of C, or (silu_mul) kBN / 128 of
       // act, each from a 64-column gate chunk and the up chunk 128 columns on.
-      // A half item holds 128 accumulator columns: two chunks of C, or one
-      // act chunk from gate columns [0, 64) and up columns [64, 128).
+      // A half item holds kBN / 2 accumulator columns: kBN / 128 chunks of
+      // C, or kBN / 256 act chunks from gate columns [0, kBN / 4) and up
+      // columns [kBN / 4, kBN / 2).
       const int out_chunks =
-          half >= 0 ? (kSiluMul ? 1 : 2) : (kSiluMul ? kBN / 128 : kBN / 64);
+          half >= 0 ? (kSiluMul ? kBN / 256 : kBN / 128) : (kSiluMul ? kBN / 128 : kBN / 64);
       const int row = store_y + lane;
       float rs = 1.f;
       if (kSiluMul && row_scale != nullptr) rs = row < M ? __ldg(row_scale + row) : 0.f;
@@ -342,8 +356,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if constexpr (kSiluMul) {
           // Interleaved weight: tile columns [256 j, 256 j + 256) hold
           // [gate block | up block] of 128 each.
-          const int gcol = half >= 0 ? 0 : (c / 2) * 256 + (c % 2) * 64;
-          const int ucol = half >= 0 ? 64 : gcol + 128;
+          const int gcol = half >= 0 ? c * 64 : (c / 2) * 256 + (c % 2) * 64;
+          const int ucol = gcol + (half >= 0 ? kBN / 4 : 128);
           uint32_t g[64], u[64];
           tmem_ld_32x32b_x32(trow + gcol, g);
           tmem_ld_32x32b_x32(trow + gcol + 32, g + 32);
@@ -354,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 64; ++j)
             f[j] = silu_f(__uint_as_float(g[j]) * rs) * (__uint_as_float(u[j]) * rs);
-          store_x = nb * (kBN / 2) + (half >= 0 ? half * 64 : c * 64);
+          store_x = nb * (kBN / 2) + (half >= 0 ? half * (kBN / 4) : 0) + c * 64;
         } else {
           uint32_t r[64];
           tmem_ld_32x32b_x32(trow + c * 64, r);
@@ -363,7 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           release_if_last(c == out_chunks - 1);
 #pragma unroll
           for (int j = 0; j < 64; ++j) f[j] = __uint_as_float(r[j]);
-          store_x = nb * kBN + (half >= 0 ? half * 128 : 0) + c * 64;
+          store_x = nb * kBN + (half >= 0 ? half * (kBN / 2) : 0) + c * 64;
         }
         if (store_x >= n_out || store_y >= M) continue;
         uint32_t pk[32];
@@ -421,11 +435,11 @@ int launch_tc2(void* c, const void* a, const void* b, const float* row_scale, in
   const int max_pairs = info.sm_count / 2;
   int pairs = tiles < max_pairs ? tiles : max_pairs;
   int tail_begin = tiles;
-  // 256-column tiles: a partial last round of at most half the pairs is cut
-  // into N halves (twice the pairs, half a tile each).
+  // A partial last round of at most half the pairs is cut into N halves
+  // (twice the pairs, half a tile each).
   const int full = tiles / max_pairs;
   const int rem = tiles - full * max_pairs;
-  if (BNP == 256 && rem > 0 && 2 * rem <= max_pairs) {
+  if (rem > 0 && 2 * rem <= max_pairs) {
     pairs = full > 0 ? max_pairs : 2 * rem;
     tail_begin = full * max_pairs;
   }

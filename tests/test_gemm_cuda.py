@@ -122,9 +122,12 @@ def test_capi_gemm_tc2(shape, dt):
 
 
 # The 256 x 512 pair tile: partial tiles in M (rows of the second CTA past M)
-# and N (the second MMA's columns past N), a single tile, several waves.
+# and N (the second MMA's columns past N), a single tile, several waves; a
+# last round of at most 37 tiles runs as N halves of 256 columns ((256, 64,
+# 512), (520, 4096, 1544), (2304, 512, 5120), (1000, 512, 4600) with a
+# ragged last half, (4096, 512, 10240) after four whole rounds).
 TC2W_SHAPES = TC_SHAPES + [(256, 64, 512), (520, 4096, 1544), (8192, 1024, 2048),
-                           (2304, 512, 5120)]
+                           (2304, 512, 5120), (1000, 512, 4600), (4096, 512, 10240)]
 
 
 @pytest.mark.parametrize("shape", TC2W_SHAPES, ids=str)
@@ -333,7 +336,8 @@ def test_split_and_whole_schedules_agree():
 
 @pytest.mark.parametrize("shape", [(256, 512, 256), (300, 328, 384), (2560, 1024, 1024),
                                    (4096, 8192, 3584), (2048, 4096, 3072), (1024, 4096, 9472),
-                                   (1000, 4096, 9344), (1000, 4096, 1280), (1000, 4096, 1024)],
+                                   (1000, 4096, 9344), (1000, 4096, 1280), (1000, 4096, 1024),
+                                   (1000, 4096, 15488)],
                          ids=str)
 def test_gemm_silu_mul_matches_oracle(shape):
     """(M, K, I): interleaved [K, 2I] weight, act [M, I]; the tails of the
@@ -343,7 +347,9 @@ def test_gemm_silu_mul_matches_oracle(shape):
     256 x 512 tiles (two gate/up block pairs; ragged M, and a last tile whose
     second pair is past 2I), (1000, 4096, 1280) on 256 x 256 pair tiles, and
     (1000, 4096, 1024) on 256 x 256 pair tiles cut into N halves (32 tiles
-    on 64 pairs: gate and up quarters stay together)."""
+    on 64 pairs: gate and up quarters stay together), and (1000, 4096,
+    15488) on 256 x 512 tiles whose last 22 run as halves of one [gate | up]
+    block each (the last tile's second block is past 2I)."""
     import torch
 
     import aot_kernel
@@ -351,7 +357,8 @@ def test_gemm_silu_mul_matches_oracle(shape):
 
     M, K, inter = shape
     expect_path = {(1024, 4096, 9472): "tc2_wide", (1000, 4096, 9344): "tc2_wide",
-                   (1000, 4096, 1280): "tc2", (1000, 4096, 1024): "tc2"}.get(shape)
+                   (1000, 4096, 1280): "tc2", (1000, 4096, 1024): "tc2",
+                   (1000, 4096, 15488): "tc2_wide"}.get(shape)
     if expect_path:
         assert capi.gemm_path(M, 2 * inter, K, 148) == expect_path
     a = randn((M, K), M + 1, "bfloat16")

@@ -114,7 +114,7 @@ def test_schedule_rejects_bad_arguments():
     ((1, 4096, 28672), "skinny"), ((128, 14336, 4096), "skinny"),
     ((8192, 8192, 8192), "tc2_wide"), ((16384, 16384, 16384), "tc2_wide"),
     ((8192, 4096, 28672), "tc2_wide"), ((4096, 8192, 57344), "tc2_wide"),
-    ((4096, 28672, 8192), "tc2"),     # 256 x 512 tiles: 3.5 rounds on 74 pairs; 256 x 256: 6.9
+    ((4096, 28672, 8192), "tc2_wide"),  # 256 x 512: 3 rounds + 34 tiles cut into halves; 256 x 256: 7
     ((4096, 4096, 4096), "tc2"),      # 256 pair tiles: 3 rounds + 34 tiles cut into halves
     ((4096, 8192, 7168), "tc"),       # the 8-way TP gate/up: 896 tiles, 8 left for K splits
     ((2048, 2048, 2048), "tc"), ((8192, 2048, 8192), "tc"),
