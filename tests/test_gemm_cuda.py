@@ -206,6 +206,11 @@ FULL = [
     (8192, 14336, 4096),
     (8192, 4096, 28672),      # the pair kernel on 256 x 512 tiles (aotk_gemm_path)
     (2048, 14336, 4096),
+    # the TP block's down GEMM per rank at W = 1 / 2 / 4: 256 x 512 pair
+    # tiles, 3 rounds on 74 pairs and 34 tiles run as 256-column halves
+    (4096, 28672, 8192),
+    (4096, 14336, 8192),
+    (4096, 7168, 8192),
 ]
 
 
@@ -337,7 +342,7 @@ def test_split_and_whole_schedules_agree():
 @pytest.mark.parametrize("shape", [(256, 512, 256), (300, 328, 384), (2560, 1024, 1024),
                                    (4096, 8192, 3584), (2048, 4096, 3072), (1024, 4096, 9472),
                                    (1000, 4096, 9344), (1000, 4096, 1280), (1000, 4096, 1024),
-                                   (1000, 4096, 15488)],
+                                   (1000, 4096, 15488), (4096, 8192, 14336)],
                          ids=str)
 def test_gemm_silu_mul_matches_oracle(shape):
     """(M, K, I): interleaved [K, 2I] weight, act [M, I]; the tails of the
@@ -349,7 +354,8 @@ def test_gemm_silu_mul_matches_oracle(shape):
     (1000, 4096, 1024) on 256 x 256 pair tiles cut into N halves (32 tiles
     on 64 pairs: gate and up quarters stay together), and (1000, 4096,
     15488) on 256 x 512 tiles whose last 22 run as halves of one [gate | up]
-    block each (the last tile's second block is past 2I)."""
+    block each (the last tile's second block is past 2I), as do the last 8
+    tiles of (4096, 8192, 14336), the TP block's gate/up per rank at W = 2."""
     import torch
 
     import aot_kernel
@@ -358,7 +364,7 @@ def test_gemm_silu_mul_matches_oracle(shape):
     M, K, inter = shape
     expect_path = {(1024, 4096, 9472): "tc2_wide", (1000, 4096, 9344): "tc2_wide",
                    (1000, 4096, 1280): "tc2", (1000, 4096, 1024): "tc2",
-                   (1000, 4096, 15488): "tc2_wide"}.get(shape)
+                   (1000, 4096, 15488): "tc2_wide", (4096, 8192, 14336): "tc2_wide"}.get(shape)
     if expect_path:
         assert capi.gemm_path(M, 2 * inter, K, 148) == expect_path
     a = randn((M, K), M + 1, "bfloat16")
