@@ -117,7 +117,8 @@ AOTK_API int aotk_rmsnorm_rstd(float* rstd, const void* x, int64_t rows, int64_t
 
 /* Tensor-core GEMM for FLOAT16 / BFLOAT16 (FLOAT32 returns AOTK_ERR_UNSUPPORTED,
  * as the reference's gemm_opt rejects it).  Picks the skinny split-K tcgen05
- * kernel (M <= 128), a CTA-pair kernel (256 x 512 or 256 x 256 tiles) or the
+ * kernel (M <= 128, except M > 96 with at least 3/4 of the SMs' worth of
+ * 256-column tiles), a CTA-pair kernel (256 x 512 or 256 x 256 tiles) or the
  * persistent 1-CTA tcgen05 kernel (whichever aotk_gemm_path names for the
  * shape) or, for shapes TMA cannot address (K or N not a multiple of 8,
  * pointers not 16-byte aligned), the SIMT kernel.

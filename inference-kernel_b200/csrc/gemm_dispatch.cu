@@ -114,7 +114,16 @@ int gemm_opt_path(int64_t M, int64_t N, int64_t K, int sm_count, bool with_works
   constexpr double kPairGain = 1.05;
   constexpr double kWideGain = 1.09;
   constexpr double kMargin = 0.98;
-  if (M <= kSkinnyMaxM) return AOTK_PATH_SKINNY;
+  if (M <= kSkinnyMaxM) {
+    // M in (96, 128]: the 1-CTA kernel (one 128-row band of tiles, B read
+    // once, no split-K reduction) beats the skinny kernel, whose cluster
+    // reduction grows with M, once its whole tiles fill 3/4 of the SMs
+    // (measured at 128 x 4096 x 28672: 54.5 vs 61.2 us; with 16-32 tiles
+    // the skinny kernel stays ahead by 1.4-1.6x).
+    const int64_t tiles = (N + 255) / 256;
+    return M > 96 && 4 * tiles >= 3 * static_cast<int64_t>(sm_count) ? AOTK_PATH_TC
+                                                                      : AOTK_PATH_SKINNY;
+  }
   if (K < 4096 || sm_count < 2) return AOTK_PATH_TC;
   int64_t sch[10];
   if (gemm_tc_schedule(M, N, K, 2, sm_count, with_workspace, sch) != AOTK_OK) return AOTK_PATH_TC;
@@ -147,12 +156,13 @@ extern "C" int aotk_gemm_opt_ws(void* c, const void* a, const void* b, int64_t M
   if (M == 0 || N == 0) return AOTK_OK;
   if (K == 0) return zero_output(c, M, N, dtype, stream);
   if (tc_eligible(c, a, b, M, N, K, dtype)) {
-    if (M <= kSkinnyMaxM) return gemm_skinny(c, a, b, M, N, K, dtype, stream);
     DeviceInfo info;
     if (int st = current_device_info(&info)) return st;
     const bool with_ws =
         workspace != nullptr && workspace_bytes >= gemm_tc_workspace_size(M, N, K, info.sm_count);
     switch (gemm_opt_path(M, N, K, info.sm_count, with_ws)) {
+      case AOTK_PATH_SKINNY:
+        return gemm_skinny(c, a, b, M, N, K, dtype, stream);
       case AOTK_PATH_TC2_WIDE:
         return gemm_tc2_wide(c, a, b, M, N, K, dtype, stream);
       case AOTK_PATH_TC2:

@@ -202,6 +202,7 @@ FULL = [
     (1, 4096, 28672),         # Llama-3-8B fused gate+up, decode
     (16, 4096, 6144),
     (128, 14336, 4096),
+    (128, 4096, 28672),       # M <= 128 on the 1-CTA kernel: 112 whole tiles, one wave
     (2048, 4096, 28672),
     (8192, 14336, 4096),
     (8192, 4096, 28672),      # the pair kernel on 256 x 512 tiles (aotk_gemm_path)

@@ -112,6 +112,9 @@ def test_schedule_rejects_bad_arguments():
 
 @pytest.mark.parametrize("shape,path", [
     ((1, 4096, 28672), "skinny"), ((128, 14336, 4096), "skinny"),
+    ((128, 4096, 6144), "skinny"),    # 24 tiles of 256 columns
+    ((128, 4096, 28672), "tc"),       # 112 tiles >= 3/4 of 148 SMs: no split-K reduction
+    ((96, 4096, 28672), "skinny"),    # M <= 96 stays on the skinny kernel
     ((8192, 8192, 8192), "tc2_wide"), ((16384, 16384, 16384), "tc2_wide"),
     ((8192, 4096, 28672), "tc2_wide"), ((4096, 8192, 57344), "tc2_wide"),
     ((4096, 28672, 8192), "tc2_wide"),  # 256 x 512: 3 rounds + 34 tiles cut into halves; 256 x 256: 7
